@@ -1,0 +1,503 @@
+"""Tree-verification benchmark: tree attention over [prefix | tree] on B200.
+
+One step is one tree-verify attention layer over a batch of sequences, run
+through the public operator ``fused_tree_verify`` (mask-free, parents only).
+The default workload is the Llama-3-8B layer shape: batch 16, 32 query / 8
+key-value heads, head_dim 128, prefix 8192, a 64-node random tree per
+sequence (depth <= 5), bf16.
+
+Prints one JSON line (rank 0).  ``value`` is algorithmic HBM GB/s summed over
+all GPUs (K and V of every sequence read once, Q read once, output written
+once, parents read once) with inputs resident in HBM; ``e2e`` is the same
+metric with each step's new inputs (Q, the tree's K/V rows, parents) copied
+from pinned host memory and the output copied back inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+    python bench.py --impl reference ...   # the CPU oracle port on host cores
+
+Multi-GPU (torchrun, one rank per GPU): each rank verifies its own batch of
+sequences (weak scaling by sequence); the timing is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import random
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import projectgorgon_b200 as G  # noqa: E402
+from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
+
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
+# dominant kernel from the ncu captures summarised under profiles/, keyed by
+# (workload, backend).  None until a capture exists.
+NCU_TRAFFIC_BYTES = {}
+
+WORKLOADS = {
+    "verify-b16-p8192-n64": dict(B=16, Hq=32, Hkv=8, D=128, P=8192, N=64, dtype="bf16",
+                                 tree="random", max_depth=5),
+    "verify-b1-p2048-n64": dict(B=1, Hq=32, Hkv=8, D=128, P=2048, N=64, dtype="bf16",
+                                tree="random", max_depth=5),
+    "ref-fp32-b1-p512-n31": dict(B=1, Hq=32, Hkv=32, D=128, P=512, N=31, dtype="fp32",
+                                 tree="cartesian", max_depth=31),
+    "ragged-b16-p1k-8k-n64": dict(B=16, Hq=32, Hkv=8, D=128, P=(1024, 8192), N=64, dtype="bf16",
+                                  tree="random", max_depth=5),
+}
+DEFAULT_WORKLOAD = "verify-b16-p8192-n64"
+TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# --------------------------------------------------------------------------
+# workload construction
+# --------------------------------------------------------------------------
+class Workload:
+    """Seeded synthetic inputs of one workload, resident on `dev`."""
+
+    def __init__(self, name: str, dev: torch.device, seed: int):
+        cfg = WORKLOADS[name]
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, Hq, Hkv, D, N = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"]
+        rng = random.Random(seed)
+        if isinstance(cfg["P"], tuple):
+            self.prefixes = [rng.randint(*cfg["P"]) for _ in range(B)]
+        else:
+            self.prefixes = [cfg["P"]] * B
+        self.ragged = isinstance(cfg["P"], tuple)
+        if cfg["tree"] == "random":
+            self.parents = [random_tree(N, rng, cfg["max_depth"]) for _ in range(B)]
+        else:
+            self.parents = [cartesian_tree(4, 2, True)] * B
+        self.max_depth = cfg["max_depth"]
+        dt = TORCH_DT[cfg["dtype"]]
+        self.dtype = dt
+        g = torch.Generator(device=dev).manual_seed(seed)
+        s = 1.0 / math.sqrt(D)
+        self.q = (torch.randn(B, Hq, N, D, device=dev, generator=g) * s).to(dt)
+        if self.ragged:
+            lens = [p + N for p in self.prefixes]
+            self.cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=dev)
+            total = int(sum(lens))
+            self.k = (torch.randn(total, Hkv, D, device=dev, generator=g) * s).to(dt)
+            self.v = (torch.randn(total, Hkv, D, device=dev, generator=g) * s).to(dt)
+            self.max_seqlen = max(lens)
+        else:
+            L = self.prefixes[0] + N
+            self.cu = None
+            self.k = torch.empty(B, Hkv, L, D, device=dev, dtype=dt)
+            self.v = torch.empty(B, Hkv, L, D, device=dev, dtype=dt)
+            for b in range(B):  # per-sequence fill keeps the fp32 temporary small
+                self.k[b] = (torch.randn(Hkv, L, D, device=dev, generator=g) * s).to(dt)
+                self.v[b] = (torch.randn(Hkv, L, D, device=dev, generator=g) * s).to(dt)
+            self.max_seqlen = L
+        self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
+        esz = torch.tensor([], dtype=dt).element_size()
+        kv_rows = sum(p + N for p in self.prefixes)
+        self.bytes = (2 * kv_rows * Hkv * D * esz + 2 * B * Hq * N * D * esz + B * N * 4
+                      + ((B + 1) * 4 if self.ragged else 0))
+        self.flops = 4 * Hq * N * D * kv_rows
+        self.tokens = B * N
+
+    def kwargs(self):
+        kw = dict(parents=self.par_t, max_depth=self.max_depth)
+        if self.ragged:
+            kw.update(cu_seqlens=self.cu, max_seqlen=self.max_seqlen)
+        return kw
+
+    def step(self):
+        return G.fused_tree_verify(self.q, self.k, self.v, **self.kwargs())
+
+    def plan(self):
+        return G.tree_attention_plan(self.q, self.k, self.v, **self.kwargs())
+
+
+# --------------------------------------------------------------------------
+# clocks during the timed region
+# --------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu_index), "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the oracle port (numpy / BLAS) on a bounded sample
+# --------------------------------------------------------------------------
+def cpu_slices(cfg: dict, count: int, seed: int = 0):
+    """`count` random (batch, q-head) slices of a workload, generated on the
+    host with the workload's shapes and distributions: (q [N, D], k, v
+    [P_b + N, D], mask [N, P_b + N], kv rows) in float32."""
+    from oracle import gorgon_oracle as O
+    rng = np.random.default_rng(seed)
+    prng = random.Random(seed)
+    N, D = cfg["N"], cfg["D"]
+    s = 1.0 / math.sqrt(D)
+    for _ in range(count):
+        P = prng.randint(*cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"]
+        par = random_tree(N, prng, cfg["max_depth"]) if cfg["tree"] == "random" else cartesian_tree(4, 2, True)
+        q = (rng.standard_normal((N, D), dtype=np.float32) * s)
+        k = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
+        v = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
+        yield q, k, v, O.prefix_tree_mask(par, P, cfg["max_depth"]), P + N
+
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        return max(int(i.get("num_threads", 1)) for i in threadpool_info()) or 1
+    except Exception:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def mean_kv_rows(cfg: dict) -> float:
+    if isinstance(cfg["P"], tuple):
+        return (cfg["P"][0] + cfg["P"][1]) / 2 + cfg["N"]
+    return cfg["P"] + cfg["N"]
+
+
+def cpu_baseline(wl: "Workload", budget_s: float = 12.0, max_slices: int = 64):
+    """Times the oracle's tree_attention on (batch, query-head) slices of the
+    workload for about `budget_s` seconds and extrapolates to the full layer
+    by key/value rows."""
+    from oracle import gorgon_oracle as O
+    cfg = wl.cfg
+    cores = blas_threads()
+    total_slices = cfg["B"] * cfg["Hq"]
+    times, rows = [], 0
+    t_start = time.perf_counter()
+    for q, k, v, m, L in cpu_slices(cfg, max_slices, seed=1):
+        t0 = time.perf_counter()
+        O.tree_attention(q, k, v, m)
+        times.append(time.perf_counter() - t0)
+        rows += L
+        if time.perf_counter() - t_start > budget_s:
+            break
+    layer_s = sum(times) / rows * (sum(p + cfg["N"] for p in wl.prefixes) / cfg["B"]) * total_slices
+    return {
+        "value": round(wl.bytes / layer_s / 1e9, 4),
+        "unit": "GB/s",
+        "cores": cores,
+        "kind": "port",
+        "us_per_layer": round(layer_s * 1e6, 1),
+        "sample": (f"{len(times)} of {total_slices} (batch, q-head) slices of this workload, "
+                   f"oracle tree_attention in fp32 numpy/BLAS on {cores} threads, "
+                   f"extrapolated by kv rows to the full layer"),
+    }
+
+
+# --------------------------------------------------------------------------
+# timing
+# --------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def time_device(wl: Workload, steps: int, warmup: int, world: int, sampler_idx: int):
+    dev = wl.dev
+    for _ in range(warmup):
+        wl.step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    st = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    with ClockSampler(sampler_idx) as clk:
+        for i in range(steps):
+            starts[i].record(st)
+            wl.step()
+            ends[i].record(st)
+        torch.cuda.synchronize(dev)
+    total_ms = starts[0].elapsed_time(ends[-1])
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if world > 1:
+        torch.distributed.barrier()
+    return total_ms, float(np.mean(per)), clk.summary()
+
+
+def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
+    """Each step: H2D of Q, the tree's K/V rows and parents from pinned host
+    memory, the tree rows written into the resident cache, the attention
+    call, and D2H of the output."""
+    dev = wl.dev
+    cfg = wl.cfg
+    B, N = cfg["B"], cfg["N"]
+    q_h = wl.q.cpu().pin_memory()
+    par_h = wl.par_t.cpu().pin_memory()
+    if wl.ragged:
+        rows = torch.cat([torch.arange(int(wl.cu[b + 1]) - N, int(wl.cu[b + 1])) for b in range(B)]).to(dev)
+        kt_h = wl.k[rows].cpu().pin_memory()
+        vt_h = wl.v[rows].cpu().pin_memory()
+    else:
+        P = wl.prefixes[0]
+        kt_h = wl.k[:, :, P:P + N].contiguous().cpu().pin_memory()
+        vt_h = wl.v[:, :, P:P + N].contiguous().cpu().pin_memory()
+    out_h = torch.empty(wl.q.shape, dtype=wl.q.dtype).pin_memory()
+    q_d = torch.empty_like(wl.q)
+    kt_d = torch.empty(kt_h.shape, dtype=kt_h.dtype, device=dev)
+    vt_d = torch.empty(vt_h.shape, dtype=vt_h.dtype, device=dev)
+    par_d = torch.empty_like(wl.par_t)
+    h2d = sum(t.numel() * t.element_size() for t in (q_h, kt_h, vt_h, par_h))
+    d2h = out_h.numel() * out_h.element_size()
+
+    def one():
+        q_d.copy_(q_h, non_blocking=True)
+        kt_d.copy_(kt_h, non_blocking=True)
+        vt_d.copy_(vt_h, non_blocking=True)
+        par_d.copy_(par_h, non_blocking=True)
+        if wl.ragged:
+            wl.k[rows] = kt_d
+            wl.v[rows] = vt_d
+        else:
+            wl.k[:, :, P:P + N].copy_(kt_d)
+            wl.v[:, :, P:P + N].copy_(vt_d)
+        kw = wl.kwargs()
+        kw["parents"] = par_d
+        o = G.fused_tree_verify(q_d, wl.k, wl.v, **kw)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        one()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1), h2d, d2h
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    G.load_library()
+    wl = Workload(args.workload, dev, seed=1000 * rank)
+    plan = wl.plan()
+    total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world, local)
+    total_ms = max_over_ranks(total_ms, world, dev)
+    launch_ms = max_over_ranks(launch_ms, world, dev)
+    e2e_ms, h2d, d2h = time_e2e(wl, args.e2e_steps or args.steps, args.warmup, world)
+    e2e_ms = max_over_ranks(e2e_ms, world, dev)
+    e2e_steps = args.e2e_steps or args.steps
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    ms_step = total_ms / args.steps
+    value = world * wl.bytes * args.steps / (total_ms * 1e-3) / 1e9
+    e2e_val = world * wl.bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    achieved = wl.bytes / (launch_ms * 1e-3) / 1e9
+    cfg = wl.cfg
+    out = {
+        "metric": "tree-verify HBM GB/s (algorithmic bytes / step time)",
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": cfg["dtype"],
+        "data": "synthetic (seeded N(0,1)/sqrt(128) q/k/v, random trees)",
+        "config": {
+            "workload": wl.name, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"], "heads_kv": cfg["Hkv"],
+            "head_dim": cfg["D"], "prefix": cfg["P"] if not wl.ragged else list(cfg["P"]),
+            "tree_nodes": cfg["N"], "max_depth": wl.max_depth, "mask": "parents (mask-free)",
+            "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+            "l2": f"inputs larger than L2 ({wl.bytes / 1e6:.0f} MB per step per GPU)",
+            "backend": plan["backend"], "splits": plan["splits"],
+        },
+        "us_per_layer": round(ms_step * 1e3, 2),
+        "pct_of_8tbs": round(100.0 * value / world / 8000.0, 2),
+        "tokens_verified_per_s": round(world * wl.tokens / (ms_step * 1e-3), 1),
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+            if peak_kind == "measured" else "fallback 6650 GB/s",
+            "traffic": NCU_TRAFFIC_BYTES.get((wl.name, plan["backend"])),
+            "launch_us": round(launch_ms * 1e3, 3),
+            "algorithmic_bytes": wl.bytes,
+            "tflops": round(wl.flops / (launch_ms * 1e-3) / 1e12, 2),
+        },
+        "e2e": {
+            "value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 5),
+            "note": "prefix K/V cache resident in HBM; per step the tree's Q, K/V rows and "
+                    "parents are copied in and the output copied out",
+        },
+        "gpu_launches": plan["launches"] * args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_budget)
+    print(json.dumps(out), flush=True)
+
+
+def run_reference(args):
+    """CPU oracle port on the host cores, same metric and workload.  Each step
+    is one (batch, q-head) slice; the layer time is extrapolated by kv rows."""
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    from oracle import gorgon_oracle as O
+    cfg = WORKLOADS[args.workload]
+    cores = blas_threads()
+    inputs = list(cpu_slices(cfg, 8, seed=0))
+    total_slices = cfg["B"] * cfg["Hq"]
+    esz = 2 if cfg["dtype"] == "bf16" else 4
+    rows = mean_kv_rows(cfg)
+    layer_bytes = (2 * rows * cfg["B"] * cfg["Hkv"] * cfg["D"] * esz
+                   + 2 * cfg["B"] * cfg["Hq"] * cfg["N"] * cfg["D"] * esz + cfg["B"] * cfg["N"] * 4)
+    for i in range(args.warmup):
+        O.tree_attention(*inputs[i % len(inputs)][:4])
+    t_layer = []
+    for i in range(args.steps):
+        q, k, v, m, L = inputs[i % len(inputs)]
+        t0 = time.perf_counter()
+        O.tree_attention(q, k, v, m)
+        t_layer.append((time.perf_counter() - t0) / L * rows * total_slices)
+    layer_s = float(np.mean(t_layer))
+    value = layer_bytes / layer_s / 1e9
+    out = {
+        "impl": "reference",
+        "metric": "tree-verify HBM GB/s (algorithmic bytes / step time)",
+        "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(layer_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
+        "config": {"workload": args.workload, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"],
+                   "heads_kv": cfg["Hkv"], "head_dim": cfg["D"],
+                   "prefix": list(cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"],
+                   "tree_nodes": cfg["N"]},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": "each step one (batch, q-head) slice of the workload through the "
+                                   "oracle's tree_attention (fp32 numpy/BLAS), extrapolated by kv "
+                                   "rows to the full layer"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=0, help="steps of the e2e loop (default: --steps)")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE={ws}; using WORLD_SIZE")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

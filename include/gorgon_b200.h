@@ -1,0 +1,216 @@
+/*
+ * gorgon_b200.h - C ABI of the B200 (sm_100a) tree-verification library.
+ *
+ * One shared library (libgorgon_b200.so) exports the entry points below.  They
+ * take plain device pointers, element strides and sizes, and a CUDA stream
+ * passed as `void*` (a cudaStream_t; NULL is the legacy default stream).  Every
+ * entry point is stream-ordered and asynchronous unless stated otherwise, and
+ * returns a gorgon_status (0 = ok).  On error, gorgon_last_error() returns a
+ * message for the calling thread.  The library never allocates device memory
+ * behind the caller's back: kernels that need scratch space take a caller-owned
+ * workspace whose size the matching *_workspace_size() function reports.
+ *
+ * Each entry point replaces one operator of ProjectGorgon's Python surface;
+ * the reference interface is cited beside it (paths are inside that project).
+ */
+#ifndef GORGON_B200_H_
+#define GORGON_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GORGON_API __attribute__((visibility("default")))
+#else
+#define GORGON_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GORGON_ABI_VERSION 1
+
+typedef enum {
+  GORGON_OK = 0,
+  GORGON_ERR_INVALID = 1,     /* bad argument: shape, stride, dtype, null pointer */
+  GORGON_ERR_UNSUPPORTED = 2, /* valid request this build cannot run */
+  GORGON_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  GORGON_ERR_WORKSPACE = 4    /* workspace missing or smaller than required */
+} gorgon_status;
+
+typedef enum {
+  GORGON_F32 = 0,
+  GORGON_BF16 = 1,
+  GORGON_F16 = 2
+} gorgon_dtype;
+
+/* How the tree rows of each sequence are masked. */
+typedef enum {
+  GORGON_MASK_PARENTS = 0,   /* ancestor walk over parents[]; prefix rows visible */
+  GORGON_MASK_DENSE = 1,     /* mask[n, mask_cols]; mask_cols == kv length of the sequence */
+  GORGON_MASK_DENSE_TREE = 2 /* mask[n, n] over the tree rows; prefix rows visible */
+} gorgon_mask_kind;
+
+typedef enum {
+  GORGON_BACKEND_AUTO = 0,   /* tensor cores when the shape allows, else CUDA cores */
+  GORGON_BACKEND_SIMT = 1,   /* CUDA-core split-K kernel (any head_dim <= 256, f32/bf16/f16) */
+  GORGON_BACKEND_TCGEN05 = 2 /* tcgen05 kernel (bf16/f16, head_dim 128) */
+} gorgon_backend;
+
+/* ABI version compiled into the library (GORGON_ABI_VERSION). */
+GORGON_API int gorgon_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+GORGON_API const char* gorgon_last_error(void);
+
+/* Reads (synchronously) the device-side error word of the current device:
+ * bit 0 = a parents[] entry outside [-1, n) was met, bit 1 = a KV-trim index
+ * outside the cache, bit 2 = a verifier tree/draft entry out of range.  The
+ * offending element is skipped, never dereferenced.  clear != 0 resets it. */
+GORGON_API int gorgon_device_error(uint32_t* out_flags, int clear);
+
+/* ------------------------------------------------------------------------
+ * Tree mask.  Replaces build_tree_mask(parents, depth)
+ * (src/gorgon/kernels/tree_mask.py:16-44) and candidate_tree_to_mask
+ * (src/gorgon/inference/tree_candidates.py:248-279).
+ * out[b, i, j] = 1 iff j == i or j is within `depth` parent hops above i
+ * (depth < 0 means n hops, the reference's default).  parents: int32
+ * [batch, n] with row stride parents_stride_b (0 = one tree for all rows);
+ * out: uint8 [batch, n, n] contiguous.  n <= 32768.
+ * ---------------------------------------------------------------------- */
+GORGON_API int gorgon_tree_mask(const int32_t* parents, int64_t batch, int64_t n,
+                     int64_t parents_stride_b, int64_t depth, uint8_t* out,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tree attention over [prefix | tree] key/value rows.
+ *
+ * Replaces tree_attention_ref / tree_attention_triton / tree_attention_cuda
+ * (src/gorgon/kernels/tree_attention_ref.py:8-18,
+ * tree_attention_triton.py:86-127, tree_attention_cuda.py:24-38 ->
+ * kernels/cuda/tree_attention.cpp:12-46) when mask_kind is DENSE or
+ * DENSE_TREE, and fused_tree_verify (fused_tree_verify_triton.py:110-172)
+ * when mask_kind is PARENTS.  The reference is one 2-D head; this call adds
+ * batch, grouped-query heads (query head h reads kv head h / (heads_q /
+ * heads_kv)), a key/value prefix and ragged sequences.
+ *
+ * Layouts (strides in elements, head_dim contiguous):
+ *   q   [batch, heads_q,  n_tree, head_dim]
+ *   k,v [batch, heads_kv, kv_len, head_dim]    (kv_len = prefix + n_tree)
+ *   out [batch, heads_q,  n_tree, head_dim]    (dtype out_dtype)
+ * With cu_seqlens (int32 [batch+1], device) sequence b owns kv rows
+ * [cu_seqlens[b], cu_seqlens[b+1]) addressed as row * k_stride_s (the batch
+ * stride is ignored); kv_len is then the largest sequence length.  The tree
+ * is always the last n_tree rows of a sequence.
+ *
+ * out = softmax(q k^T * scale + mask) v, scale = 1/sqrt(head_dim) when
+ * scale == 0.  A row with no visible key yields NaN (as torch.softmax does).
+ * lse (optional, float [batch, heads_q, n_tree]) receives the natural-log
+ * sum of exponentials of the scaled, masked scores.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t dtype;      /* gorgon_dtype of q, k, v */
+  int32_t out_dtype;  /* gorgon_dtype of out */
+  int64_t batch, heads_q, heads_kv, n_tree, kv_len, head_dim;
+  const void* q;  int64_t q_stride_b, q_stride_h, q_stride_n;
+  const void* k;  int64_t k_stride_b, k_stride_h, k_stride_s;
+  const void* v;  int64_t v_stride_b, v_stride_h, v_stride_s;
+  void* out;      int64_t o_stride_b, o_stride_h, o_stride_n;
+  const int32_t* cu_seqlens;      /* nullable */
+  int32_t mask_kind;              /* gorgon_mask_kind */
+  const int32_t* parents;         /* PARENTS: int32 [batch, n_tree] */
+  int64_t parents_stride_b;       /*   0 = one tree shared by the batch */
+  int32_t max_depth;              /*   hops walked; < 0 = n_tree */
+  const uint8_t* mask;            /* DENSE*: uint8/bool [batch, n_tree, mask_cols] */
+  int64_t mask_stride_b, mask_stride_n;
+  float scale;
+  float* lse;                     /* nullable */
+  int32_t backend;                /* gorgon_backend */
+  int32_t num_splits;             /* 0 = chosen by the library */
+} gorgon_tree_attn_params;
+
+GORGON_API size_t gorgon_tree_attn_workspace_size(const gorgon_tree_attn_params* p);
+GORGON_API int gorgon_tree_attn(const gorgon_tree_attn_params* p, void* workspace,
+                     size_t workspace_bytes, void* stream);
+/* The launch plan gorgon_tree_attn would use for `p`: backend (gorgon_backend
+ * value actually run), key/value splits, and kernel launches per call. */
+GORGON_API int gorgon_tree_attn_plan(const gorgon_tree_attn_params* p, int32_t* backend,
+                          int32_t* splits, int32_t* launches);
+
+/* ------------------------------------------------------------------------
+ * Fused tree verifier: per-row argmax over the vocabulary, draft match and
+ * longest accepted path in one launch, with no host synchronisation.
+ * Replaces the vectorised verifier of _verify_tree_candidates
+ * (src/gorgon/inference/gorgon_loop.py:328-392, paths from
+ * get_tree_paths, src/gorgon/inference/tree_candidates.py:282-311) and, for a
+ * chain tree, accept_draft_tokens (gorgon_loop.py:161-184).
+ *
+ * Rows: node t is checked against the argmax of row prompt_len - 1 when it is
+ * a root (parent -1) and of row prompt_len + parent otherwise.  The winner is
+ * the first root-to-leaf path in DFS order (roots ascending, children in index
+ * order) with the longest accepted prefix; bonus = argmax of row
+ * prompt_len + last accepted node, or of row prompt_len - 1 when nothing is
+ * accepted (-1 if that row is beyond `rows`).  argmax returns the first index
+ * of the maximum; NaN counts as the maximum.
+ *
+ * logits [batch, rows, vocab] (vocab contiguous); draft, parents int32
+ * [batch, n] (parents_stride_b 0 = shared tree).  Outputs (int32, device):
+ * pred [batch, n + 1] = argmax of rows prompt_len - 1 + j (-1 past `rows`),
+ * accepted_len [batch], path [batch, n] (winning nodes from the root, -1
+ * padded), bonus [batch], best_node [batch] (-1 if none), hidden_row [batch]
+ * (nullable).  n <= 4096.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t dtype;  /* gorgon_dtype of logits */
+  const void* logits; int64_t logits_stride_b, logits_stride_r;
+  int64_t batch, rows, vocab, n, prompt_len;
+  const int32_t* draft;   int64_t draft_stride_b;
+  const int32_t* parents; int64_t parents_stride_b;
+  int32_t* pred;
+  int32_t* accepted_len;
+  int32_t* path;
+  int32_t* bonus;
+  int32_t* best_node;
+  int32_t* hidden_row;
+} gorgon_verify_params;
+
+GORGON_API size_t gorgon_verify_workspace_size(const gorgon_verify_params* p);
+GORGON_API int gorgon_verify(const gorgon_verify_params* p, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * KV-cache trim-on-reject for all layers in one launch.  Replaces
+ * apply_cache_slice (src/gorgon/inference/kv_cache.py:89-108) and the
+ * cache crop after verification (src/gorgon/inference/gorgon_loop.py:569-570,
+ * kv_cache.py:72-80):
+ *   dst[l][b, h, dst_start[b] + r] = src[l][b, h, src_idx[b, r]],  r < lens[b]
+ * for every layer l, batch row b, kv head h, on caches laid out
+ * [batch, heads, seq_capacity, head_dim] (strides in elements, head_dim
+ * contiguous, identical for every layer and for K and V).  k_src / v_src are
+ * HOST arrays of `layers` device pointers; k_dst / v_dst likewise, or NULL to
+ * trim in place (all rows of a (layer, b, h) slice are read before any is
+ * written, so in-place gathers whose source and destination rows overlap
+ * are safe).  src_idx int32 [batch, max_len] (row stride idx_stride_b),
+ * lens int32 [batch], dst_start int32 [batch] or NULL for 0: device arrays,
+ * so a verifier's output can feed this call without a host round trip.
+ * max_len <= 256.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t elem_bytes;  /* 1, 2, 4 or 8 */
+  int64_t layers, batch, heads, seq_capacity, head_dim;
+  int64_t stride_b, stride_h, stride_s;
+  void* const* k_src; void* const* v_src;
+  void* const* k_dst; void* const* v_dst;
+  const int32_t* src_idx; int64_t idx_stride_b, max_len;
+  const int32_t* lens;
+  const int32_t* dst_start;
+} gorgon_kv_trim_params;
+
+GORGON_API int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GORGON_B200_H_ */

@@ -1,0 +1,6 @@
+"""Verifier and KV-cache operators under ProjectGorgon's names (``gorgon.inference``)."""
+from .kv_cache import GorgonKVCache, apply_cache_slice
+from .verify import TreeVerifyResult, accept_draft_tokens, verify_tree
+
+__all__ = ["GorgonKVCache", "apply_cache_slice", "TreeVerifyResult", "accept_draft_tokens",
+           "verify_tree"]
