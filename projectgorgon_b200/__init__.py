@@ -14,10 +14,10 @@ sm_100a behind a C ABI, ``include/gorgon_b200.h``).  Host tensors raise
 from . import _abi
 from .inference import GorgonKVCache, TreeVerifyResult, accept_draft_tokens, apply_cache_slice, verify_tree
 from .kernels import (build_tree_mask, candidate_tree_to_mask, fused_tree_verify, tree_attention,
-                      tree_attention_cuda, tree_attention_triton)
+                      tree_attention_cuda, tree_attention_plan, tree_attention_triton)
 
 __all__ = [
-    "build_tree_mask", "candidate_tree_to_mask", "tree_attention", "tree_attention_cuda",
+    "build_tree_mask", "candidate_tree_to_mask", "tree_attention", "tree_attention_plan", "tree_attention_cuda",
     "tree_attention_triton", "fused_tree_verify", "verify_tree", "accept_draft_tokens",
     "apply_cache_slice", "GorgonKVCache", "TreeVerifyResult", "device_error", "load_library",
 ]

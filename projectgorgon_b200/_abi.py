@@ -48,6 +48,7 @@ class TreeAttnParams(Structure):
         ("lse", c_void_p),
         ("backend", c_int32),
         ("num_splits", c_int32),
+        ("kv_rows", c_int64),
     ]
 
 

@@ -26,6 +26,7 @@ struct AttnArgs {
   float* part_o;    // [splits, batch*hq*n, d] when splits > 1
   float* part_lse;  // [splits, batch*hq*n]   (log2 domain)
   uint32_t* err;
+  int64_t kv_rows;   // rows of k/v with cu_seqlens (0 = unknown)
   int batch, hq, hkv, group, n, kv_len, d;
   int mask_kind, max_depth, out_dtype, splits;
   int vec_ok;        // 16-byte vector loads of q/k/v rows are legal

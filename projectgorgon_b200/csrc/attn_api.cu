@@ -60,6 +60,7 @@ int make_args(const gorgon_tree_attn_params* p, AttnArgs* a) {
   x.v_sb = p->v_stride_b; x.v_sh = p->v_stride_h; x.v_ss = p->v_stride_s;
   x.o_sb = p->o_stride_b; x.o_sh = p->o_stride_h; x.o_sn = p->o_stride_n;
   x.cu_seqlens = p->cu_seqlens;
+  x.kv_rows = p->cu_seqlens ? p->kv_rows : 0;
   x.parents = p->parents; x.par_sb = p->parents_stride_b;
   x.mask = p->mask; x.mask_sb = p->mask_stride_b; x.mask_sn = p->mask_stride_n;
   x.lse = p->lse;

@@ -39,8 +39,8 @@ class TreeVerifyResult:
     def accepted_tokens(self, draft: torch.Tensor) -> List[List[int]]:
         """Host lists of accepted token ids per batch row (synchronises)."""
         d = draft if draft.dim() == 2 else draft.unsqueeze(0)
-        lens = self.accepted_len.tolist()
-        paths = self.path.tolist()
+        lens = self.accepted_len.reshape(-1).tolist()
+        paths = self.path.reshape(len(lens), -1).tolist()
         dl = d.tolist()
         return [[dl[b][paths[b][i]] for i in range(lens[b])] for b in range(len(lens))]
 

@@ -212,5 +212,6 @@ def _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, sca
     p.lse = ptr(lse)
     p.backend = _BACKENDS[backend]
     p.num_splits = int(num_splits)
+    p.kv_rows = kk.shape[0] if cu is not None else 0
     keep += [q4, kk, vv, cu]
     return _Prepared(p, out, lse, keep)

@@ -1,0 +1,141 @@
+"""The tcgen05 tree-attention kernel against the oracle (small shapes) and
+against the CUDA-core kernel (large shapes), forcing backend="tcgen05".
+
+Tolerance: bf16/f16 outputs within 2e-3 abs / 1e-2 rel of an fp32 oracle on
+the same rounded inputs."""
+from __future__ import annotations
+
+import math
+import random
+
+import numpy as np
+import pytest
+import torch
+
+import projectgorgon_b200 as G
+from oracle import gorgon_oracle as O
+from projectgorgon_b200.trees import best_first_tree, random_tree
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _inputs(B, Hq, Hkv, N, L, D=128, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    s = 1.0 / math.sqrt(D)
+    q = (torch.randn(B, Hq, N, D, device="cuda", generator=g) * s).to(dtype)
+    k = (torch.randn(B, Hkv, L, D, device="cuda", generator=g) * s).to(dtype)
+    v = (torch.randn(B, Hkv, L, D, device="cuda", generator=g) * s).to(dtype)
+    return q, k, v
+
+
+def _trees(B, N, seed, depth=5):
+    rng = random.Random(seed)
+    return [random_tree(N, rng, depth) for _ in range(B)]
+
+
+@pytest.fixture(autouse=True)
+def _no_device_errors():
+    G.device_error(clear=True)
+    yield
+    torch.cuda.synchronize()
+    assert G.device_error(clear=True) == 0
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,P", [
+    (1, 32, 8, 64, 2048),    # 2 M-tiles, pairs split across many CTAs
+    (2, 32, 8, 64, 1000),    # prefix not a multiple of the 64-row tile
+    (1, 4, 1, 7, 130),       # one partly filled M-tile
+    (1, 8, 2, 100, 300),     # 400 packed rows: two query groups
+    (1, 2, 2, 256, 500),     # 256-node tree (8 ancestor words)
+    (2, 4, 4, 64, 0),        # no prefix
+    (1, 32, 8, 1, 70),       # single node
+])
+def test_tc_matches_oracle(B, Hq, Hkv, N, P):
+    pars = _trees(B, N, seed=N + P)
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, seed=P)
+    par_t = torch.tensor(pars, device="cuda")
+    plan = G.tree_attention_plan(q, k, v, parents=par_t, max_depth=5, backend="tcgen05")
+    assert plan["backend"] == "tcgen05"
+    out = G.tree_attention(q, k, v, parents=par_t, max_depth=5, backend="tcgen05")
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=np.array(pars), max_depth=5)
+    np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_tc_lse_and_fp32_output():
+    B, Hq, Hkv, N, P = 2, 8, 2, 40, 777
+    pars = _trees(B, N, seed=5)
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, seed=5)
+    out, lse = G.tree_attention(q, k, v, parents=torch.tensor(pars, device="cuda"), max_depth=5,
+                                backend="tcgen05", out_dtype=torch.float32, return_lse=True)
+    _, lse_s = G.tree_attention(q, k, v, parents=torch.tensor(pars, device="cuda"), max_depth=5,
+                                backend="simt", return_lse=True)
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=np.array(pars), max_depth=5)
+    assert out.dtype == torch.float32
+    np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(_np(lse), _np(lse_s), atol=2e-3, rtol=1e-4)
+
+
+def test_tc_float16_and_dense_tree_mask():
+    B, Hq, Hkv, N, P = 1, 16, 4, 48, 600
+    par = _trees(1, N, seed=9)[0]
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, dtype=torch.float16, seed=9)
+    m = G.build_tree_mask(par)
+    out = G.tree_attention(q, k, v, m, backend="tcgen05")
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=par)
+    np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_tc_ragged_cu_seqlens():
+    rng = random.Random(11)
+    B, Hq, Hkv, N, D = 5, 32, 8, 64, 128
+    Ls = [rng.randint(64, 3000) + N for _ in range(B)]
+    cu = np.concatenate([[0], np.cumsum(Ls)]).astype(np.int32)
+    pars = _trees(B, N, seed=11)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    s = 1 / math.sqrt(D)
+    q = (torch.randn(B, Hq, N, D, device="cuda", generator=g) * s).bfloat16()
+    kp = (torch.randn(int(cu[-1]), Hkv, D, device="cuda", generator=g) * s).bfloat16()
+    vp = (torch.randn(int(cu[-1]), Hkv, D, device="cuda", generator=g) * s).bfloat16()
+    kw = dict(parents=torch.tensor(pars, device="cuda"), max_depth=5,
+              cu_seqlens=torch.from_numpy(cu).cuda(), max_seqlen=max(Ls))
+    assert G.tree_attention_plan(q, kp, vp, **kw, backend="tcgen05")["backend"] == "tcgen05"
+    out = G.tree_attention(q, kp, vp, **kw, backend="tcgen05")
+    for b in range(B):
+        kb = _np(kp[cu[b]:cu[b + 1]]).transpose(1, 0, 2)[None]
+        vb = _np(vp[cu[b]:cu[b + 1]]).transpose(1, 0, 2)[None]
+        ref = O.tree_attention_batched(_np(q[b:b + 1]), kb, vb, parents=pars[b], max_depth=5)
+        np.testing.assert_allclose(_np(out[b:b + 1]), ref, atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("B,P", [(16, 8192), (3, 5000)])
+def test_tc_matches_simt_at_scale(B, P):
+    """Llama-3-8B shape (32 q / 8 kv heads, d 128, 64-node trees): the
+    tensor-core kernel against the CUDA-core kernel on the same inputs."""
+    N = 64
+    pars = torch.tensor(_trees(B, N, seed=B), device="cuda")
+    q, k, v = _inputs(B, 32, 8, N, P + N, seed=B)
+    a = G.fused_tree_verify(q, k, v, pars, max_depth=5, backend="tcgen05")
+    b = G.fused_tree_verify(q, k, v, pars, max_depth=5, backend="simt")
+    torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
+
+
+def test_tc_wide_best_first_tree():
+    """256-node best-first tree (top-k 4 over 4 levels), one kv head."""
+    par, _ = best_first_tree(random.Random(0), 4, 4, 256)
+    q, k, v = _inputs(1, 4, 1, 256, 1024 + 256, seed=3)
+    out = G.tree_attention(q, k, v, parents=par, max_depth=8, backend="tcgen05")
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=par, max_depth=8)
+    np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_auto_picks_tensor_cores_for_64_node_trees():
+    q, k, v = _inputs(1, 32, 8, 64, 512)
+    par = _trees(1, 64, 0)[0]
+    assert G.tree_attention_plan(q, k, v, parents=par)["backend"] == "tcgen05"
+    q2, k2, v2 = _inputs(1, 32, 8, 31, 512)
+    assert G.tree_attention_plan(q2, k2, v2, parents=_trees(1, 31, 0)[0])["backend"] == "simt"
