@@ -25,7 +25,6 @@ import json
 import math
 import os
 import random
-import subprocess
 import sys
 import threading
 import time
@@ -130,59 +129,71 @@ class Workload:
 # clocks during the timed region
 # --------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and clock-event reasons of one GPU every few ms while
+    the timed region runs (NVML; falls back to nvidia-smi when absent)."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
-        self.proc = None
-        self.lines = []
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, dev: torch.device, period_s: float = 0.005):
+        self.dev, self.period = dev, period_s
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        try:
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.dev.index or 0)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.gpu_index), "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            h = self._handle()
+            nv = self._nvml
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                                  getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        rs = int(get_reasons(h)) if get_reasons else 0
+                        self.samples.append((mhz, rs))
+                    except Exception:
+                        pass
+                    self._stop.wait(self.period)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception as exc:  # pragma: no cover - NVML missing
+            log(f"clock sampling unavailable: {exc}")
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=2)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "nvml"}
 
 
 # --------------------------------------------------------------------------
@@ -260,7 +271,7 @@ def dist_setup():
     return world, rank, local
 
 
-def time_device(wl: Workload, steps: int, warmup: int, world: int, sampler_idx: int):
+def time_device(wl: Workload, steps: int, warmup: int, world: int):
     dev = wl.dev
     for _ in range(warmup):
         wl.step()
@@ -271,7 +282,7 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int, sampler_idx: 
     st = torch.cuda.current_stream(dev)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    with ClockSampler(sampler_idx) as clk:
+    with ClockSampler(dev) as clk:
         for i in range(steps):
             starts[i].record(st)
             wl.step()
@@ -369,7 +380,7 @@ def run_ours(args):
     G.load_library()
     wl = Workload(args.workload, dev, seed=1000 * rank)
     plan = wl.plan()
-    total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world, local)
+    total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
     total_ms = max_over_ranks(total_ms, world, dev)
     launch_ms = max_over_ranks(launch_ms, world, dev)
     e2e_ms, h2d, d2h = time_e2e(wl, args.e2e_steps or args.steps, args.warmup, world)
