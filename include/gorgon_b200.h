@@ -181,6 +181,26 @@ GORGON_API size_t gorgon_verify_workspace_size(const gorgon_verify_params* p);
 GORGON_API int gorgon_verify(const gorgon_verify_params* p, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* The fused verifier above for callers that cannot allocate device memory.
+ * No counterpart in the reference (its verifier is torch code).
+ *
+ * Some callers cannot call cudaMalloc: host runtimes that only receive the
+ * buffers an owning framework hands them (a cgo/JNI host, a serving engine
+ * whose memory comes from a fixed arena), or code that must not add a
+ * synchronising allocation to its decode step.  This entry point takes the
+ * same inputs and outputs as gorgon_verify but no workspace: its scratch (one
+ * arrival counter per sequence) is a 16 KiB array compiled into the library,
+ * held by every GPU that loads it until the process exits.
+ *
+ * - batch may be at most 4096; larger batches return GORGON_ERR_UNSUPPORTED.
+ * - The first call on a device looks up the array's address on that device
+ *   (with it current); make that first call before any stream capture.
+ * - Every call clears the counters it uses on `stream` first.  All calls
+ *   share the one array, so calls that overlap on the GPU (on different
+ *   streams at the same time) race; keep them ordered on one stream.
+ * - It allocates nothing: no cudaMalloc, cudaFree or allocating routine. */
+GORGON_API int gorgon_verify_noalloc(const gorgon_verify_params* p, void* stream);
+
 /* ------------------------------------------------------------------------
  * KV-cache trim-on-reject for all layers in one launch.  Replaces
  * apply_cache_slice (src/gorgon/inference/kv_cache.py:89-108) and the

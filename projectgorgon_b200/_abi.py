@@ -91,6 +91,7 @@ SIGNATURES = {
                                       POINTER(c_int32)]),
     "gorgon_verify_workspace_size": (c_size_t, [POINTER(VerifyParams)]),
     "gorgon_verify": (c_int, [POINTER(VerifyParams), c_void_p, c_size_t, c_void_p]),
+    "gorgon_verify_noalloc": (c_int, [POINTER(VerifyParams), c_void_p]),
     "gorgon_kv_trim": (c_int, [POINTER(KvTrimParams), c_void_p]),
 }
 

@@ -18,6 +18,7 @@
 // sibling indices there.  Nodes that never reach a root (a cycle) belong to no
 // path, as in the reference's get_tree_paths, and are never accepted.
 #include <climits>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -275,6 +276,95 @@ extern "C" int gorgon_verify(const gorgon_verify_params* p, void* workspace, siz
   a.pred = p->pred; a.accepted_len = p->accepted_len; a.path = p->path; a.bonus = p->bonus;
   a.best_node = p->best_node; a.hidden_row = p->hidden_row;
   a.counters = static_cast<int32_t*>(workspace);
+  a.err = device_error_word();
+  const int64_t ev = static_cast<int64_t>(16 / dtype_bytes(p->dtype));
+  a.vec_ok = (reinterpret_cast<uintptr_t>(p->logits) % 16 == 0) && p->logits_stride_b % ev == 0 &&
+             p->logits_stride_r % ev == 0;
+  const int batch = static_cast<int>(p->batch);
+  switch (p->dtype) {
+    case GORGON_F32: return launch_verify_t<float>(a, batch, st);
+    case GORGON_BF16: return launch_verify_t<__nv_bfloat16>(a, batch, st);
+    default: return launch_verify_t<__half>(a, batch, st);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// gorgon_verify_noalloc: the same fused verifier for callers that cannot
+// allocate device memory.  Its only scratch, one arrival counter per sequence,
+// lives in a fixed array compiled into the library instead of a caller
+// workspace.  Every GPU that loads the library holds this array until the
+// process exits.
+namespace gorgon {
+namespace {
+
+constexpr int kNoAllocMaxBatch = 4096;  // 16 KiB of counters per device
+
+static __device__ __align__(256) int32_t g_verify_noalloc_counters[kNoAllocMaxBatch];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+int32_t* g_noalloc_counters[kNoAllocMaxDevices] = {};
+
+// Device address of the counter array on the current device.  Host code only
+// sees a stand-in for a __device__ symbol, so the address is looked up once
+// per device (with that device current) and cached.
+int noalloc_counters(int32_t** out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "gorgon_verify_noalloc: cudaGetDevice");
+  if (rc) return rc;
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_verify_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_counters[dev]) {
+    void* p = nullptr;
+    rc = check_cuda(cudaGetSymbolAddress(&p, g_verify_noalloc_counters),
+                    "gorgon_verify_noalloc: cudaGetSymbolAddress");
+    if (rc) return rc;
+    g_noalloc_counters[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_counters[dev];
+  return GORGON_OK;
+}
+
+}  // namespace
+}  // namespace gorgon
+
+extern "C" int gorgon_verify_noalloc(const gorgon_verify_params* p, void* stream) {
+  using namespace gorgon;
+  if (!p) return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: params is null");
+  if (!dtype_ok(p->dtype)) return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: unknown dtype");
+  if (p->batch < 0 || p->rows < 0 || p->vocab < 0 || p->n < 0)
+    return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: negative size");
+  if (p->batch == 0) return GORGON_OK;
+  if (p->batch > kNoAllocMaxBatch)
+    return set_error(GORGON_ERR_UNSUPPORTED,
+                     "gorgon_verify_noalloc: batch > 4096; its fixed scratch holds 4096 sequence counters "
+                     "(use gorgon_verify with a workspace for larger batches)");
+  if (p->n < 1 || p->n > 4096) return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_verify_noalloc: n must be in [1, 4096]");
+  if (p->prompt_len < 1) return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: prompt_len must be >= 1");
+  if (p->vocab < 1 || p->vocab > INT_MAX - 16)
+    return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: vocab outside [1, 2^31)");
+  if (p->rows < p->prompt_len) return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: rows < prompt_len");
+  if (!p->logits || !p->draft || !p->parents || !p->pred || !p->accepted_len || !p->path || !p->bonus ||
+      !p->best_node)
+    return set_error(GORGON_ERR_INVALID, "gorgon_verify_noalloc: null pointer");
+  int32_t* counters = nullptr;
+  int rc = noalloc_counters(&counters);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's counts: clear the ones this call uses.
+  rc = check_cuda(cudaMemsetAsync(counters, 0, static_cast<size_t>(p->batch) * sizeof(int32_t), st),
+                  "gorgon_verify_noalloc counter reset");
+  if (rc) return rc;
+  VerifyArgs a{};
+  a.logits = p->logits; a.lsb = p->logits_stride_b; a.lsr = p->logits_stride_r;
+  a.rows = p->rows; a.vocab = p->vocab;
+  a.n = static_cast<int>(p->n); a.prompt_len = static_cast<int>(p->prompt_len);
+  a.draft = p->draft; a.dsb = p->draft_stride_b;
+  a.parents = p->parents; a.psb = p->parents_stride_b;
+  a.pred = p->pred; a.accepted_len = p->accepted_len; a.path = p->path; a.bonus = p->bonus;
+  a.best_node = p->best_node; a.hidden_row = p->hidden_row;
+  a.counters = counters;
   a.err = device_error_word();
   const int64_t ev = static_cast<int64_t>(16 / dtype_bytes(p->dtype));
   a.vec_ok = (reinterpret_cast<uintptr_t>(p->logits) % 16 == 0) && p->logits_stride_b % ev == 0 &&
