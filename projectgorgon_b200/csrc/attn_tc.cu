@@ -12,15 +12,17 @@
 // finishes it last merges them (no spinning: an atomic arrival count).
 //
 // Warp roles (384 threads):
-//   warp 0       TMA producer: K and V tiles (two 64-column SW128 boxes each)
-//                into a 3-stage ring
-//   warp 1       MMA issuer (one thread): S = Q K^T into TMEM, O += P V
+//   warp 0       TMA producer for K tiles (two 64-column SW128 boxes), 5-stage ring
+//   warp 3       TMA producer for V tiles, its own 5-stage ring
+//   warp 1       MMA issuer (one thread): S = Q K^T into TMEM, O += P V with P
+//                read from TMEM; it never holds P.V(i) back behind K(i + 1)
 //   warp 2       TMEM allocation / release
 //   warps 4-7    softmax + epilogue of M-tile 0 (TMEM lanes 0-127)
 //   warps 8-11   softmax + epilogue of M-tile 1
 // TMEM (512 columns): S double-buffered (2 buffers x 2 M-tiles x 64 columns),
-// O (2 M-tiles x 128 columns).  P goes back through shared memory (bf16,
-// SW128 K-major) as the A operand of the P.V MMA.
+// O (2 M-tiles x 128 columns).  P (bf16, two per 32-bit column) overwrites the
+// first 32 columns of its own S buffer and is the TMEM A operand of P.V.
+// A K stage is released as soon as its Q.K^T completes, a V stage after P.V.
 //
 // Softmax per row is owned by one thread (TMEM lane = row), so row max and
 // sum need no shuffles.  Rescaling of O is lazy: the running max only moves
@@ -46,19 +48,18 @@ constexpr int kBM = 128;              // rows per MMA tile
 constexpr int kQRows = 2 * kBM;       // packed query rows per pair
 constexpr int kBN = 64;               // key/value rows per tile
 constexpr int kD = 128;               // head_dim
-constexpr int kStages = 3;
+constexpr int kStages = 5;             // per ring (K and V)
 constexpr int kThreads = 384;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr long long kWaitLimitCycles = 4000000000ll;  // about 2 s at the boost clock
 
 // shared memory layout (bytes from a 1024-aligned base)
 constexpr uint32_t kQHalf = kBM * 128;                 // 128 rows x 64 cols bf16 = 16 KB
 constexpr uint32_t kKVHalf = kBN * 128;                // 64 rows x 64 cols = 8 KB
-constexpr uint32_t kStageBytes = 4 * kKVHalf;          // K and V, two halves each
-constexpr uint32_t kPTile = kBM * kBN * 2;             // 128 x 64 bf16 = 16 KB
+constexpr uint32_t kTileBytes = 2 * kKVHalf;           // one K or V tile, two halves
 constexpr uint32_t kOffQ = 0;                          // [mtile][half]
-constexpr uint32_t kOffKV = kOffQ + 4 * kQHalf;        // [stage][K0 K1 V0 V1]
-constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;  // [buf][mtile]
-constexpr uint32_t kOffBar = kOffP + 4 * kPTile;
+constexpr uint32_t kOffK = kOffQ + 4 * kQHalf;         // [stage][half]
+constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
+constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + alignment slack
 
 // TMEM columns
@@ -82,16 +83,19 @@ struct TcArgs {
 };
 
 struct Barriers {
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
   uint64_t q_full;
   uint64_t s_full[2];
   uint64_t p_full[2];
-  uint64_t p_free[2];
+  uint64_t p_free[2];  // P.V of the tile in this buffer has completed
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 // ------------------------------------------------------------ schedule
 __device__ __forceinline__ int64_t total_tiles(const TcArgs& t) {
@@ -147,24 +151,31 @@ __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
 }
 
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  return mbar_wait(bar, parity, abort, kWaitLimitNs);
+  return mbar_wait(bar, parity, abort, kWaitLimitCycles);
 }
 
-// Wait used on the way out: ignores the abort flag, gives up after 100 ms.
+// Wait used on the way out: ignores the abort flag, gives up after about 100 ms.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > 100000000ull) break;
+    if (clock64() - t0 > 200000000ll) break;
   }
 }
 
 // ------------------------------------------------------------ roles
-__device__ void producer(const TcArgs& t, const CUtensorMap* kmap, const CUtensorMap* vmap, uint8_t* smem,
-                         Barriers* bars, int64_t g0, int64_t g1) {
+// Streams one operand (K when is_v == 0, else V) of every tile in [g0, g1)
+// through its ring.
+__device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem, Barriers* bars, int64_t g0,
+                         int64_t g1, int is_v) {
   volatile int* abort = &bars->abort;
+  uint64_t* full = is_v ? bars->v_full : bars->k_full;
+  uint64_t* empty = is_v ? bars->v_empty : bars->k_empty;
+  uint8_t* ring = smem + (is_v ? kOffV : kOffK);
   int64_t issued = 0;
   int cur_pair = -1;
   PairInfo pi{};
+  // K/V are read once: keep them from pushing the partial results out of L2
+  const uint64_t policy = l2_policy_evict_first();
   for (int64_t g = g0; g < g1; ++g) {
     const int p = pair_of(t, g);
     if (p != cur_pair) {
@@ -174,104 +185,150 @@ __device__ void producer(const TcArgs& t, const CUtensorMap* kmap, const CUtenso
     const int tile = static_cast<int>(g - pi.start);
     const int stage = static_cast<int>(issued % kStages);
     const uint32_t ph = static_cast<uint32_t>(issued / kStages) & 1u;
-    if (!bounded_wait(&bars->kv_empty[stage], ph ^ 1u, abort)) break;
-    mbar_arrive_expect_tx(&bars->kv_full[stage], kStageBytes);
-    uint8_t* st = smem + kOffKV + stage * kStageBytes;
+    if (!bounded_wait(&empty[stage], ph ^ 1u, abort)) break;
+    mbar_arrive_expect_tx(&full[stage], kTileBytes);
+    uint8_t* st = ring + stage * kTileBytes;
     const int row = tile * kBN;
     if (t.varlen) {
       const int r = pi.row0 + row;
-      tma_load_3d(st + 0 * kKVHalf, kmap, &bars->kv_full[stage], 0, pi.kvh, r);
-      tma_load_3d(st + 1 * kKVHalf, kmap, &bars->kv_full[stage], 64, pi.kvh, r);
-      tma_load_3d(st + 2 * kKVHalf, vmap, &bars->kv_full[stage], 0, pi.kvh, r);
-      tma_load_3d(st + 3 * kKVHalf, vmap, &bars->kv_full[stage], 64, pi.kvh, r);
+      tma_load_3d_hint(st, map, &full[stage], 0, pi.kvh, r, policy);
+      tma_load_3d_hint(st + kKVHalf, map, &full[stage], 64, pi.kvh, r, policy);
     } else {
-      tma_load_4d(st + 0 * kKVHalf, kmap, &bars->kv_full[stage], 0, row, pi.kvh, pi.b);
-      tma_load_4d(st + 1 * kKVHalf, kmap, &bars->kv_full[stage], 64, row, pi.kvh, pi.b);
-      tma_load_4d(st + 2 * kKVHalf, vmap, &bars->kv_full[stage], 0, row, pi.kvh, pi.b);
-      tma_load_4d(st + 3 * kKVHalf, vmap, &bars->kv_full[stage], 64, row, pi.kvh, pi.b);
+      tma_load_4d_hint(st, map, &full[stage], 0, row, pi.kvh, pi.b, policy);
+      tma_load_4d_hint(st + kKVHalf, map, &full[stage], 64, row, pi.kvh, pi.b, policy);
     }
     ++issued;
   }
   // Every issued load must land before the CTA leaves.
   for (int64_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
-    drain_wait(&bars->kv_full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u);
+    drain_wait(&full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u);
+}
+
+// Ring position of a tile counter, advanced without divisions.
+struct Ring {
+  uint32_t stage = 0, phase = 0;
+  __device__ __forceinline__ void next() {
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// The MMA issuer keeps every operand descriptor in registers and only adds
+// constant offsets (in the descriptor's 16-byte address units) per K step.
+struct MmaDescs {
+  uint64_t q[2][2];  // [mtile][d half], SW128 K-major, SBO 1 KB
+  uint64_t k0;       // K ring stage 0, half 0
+  uint64_t v0;       // V ring stage 0: MN-major, LBO 8 KB (d halves), SBO 1 KB
+  uint32_t idesc_qk, idesc_pv;
+};
+
+// S = Q K^T of one tile into S buffer `buf`, both M-tiles.
+__device__ __forceinline__ void issue_qk(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf) {
+  const uint64_t kst = md.k0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const uint32_t d_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
+#pragma unroll
+    for (int ks = 0; ks < kD / 16; ++ks) {
+      const uint64_t a = md.q[mt][ks >> 2] + static_cast<uint64_t>((ks & 3) * 2);
+      const uint64_t b = kst + static_cast<uint64_t>((ks >> 2) * (kKVHalf >> 4) + (ks & 3) * 2);
+      umma_f16_ss(d_tmem, a, b, md.idesc_qk, ks > 0 ? 1u : 0u);
+    }
+  }
+}
+
+// O_mt += P_mt (TMEM, over S buffer `buf`) * V (smem stage).
+__device__ __forceinline__ void issue_pv(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf,
+                                         uint32_t first) {
+  const uint64_t vst = md.v0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+    const uint32_t d_tmem = tmem + kColO + mt * kD;
+    const uint32_t p_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
+#pragma unroll
+    for (int ks = 0; ks < kBN / 16; ++ks) {
+      umma_f16_ts(d_tmem, p_tmem + ks * 8, vst + static_cast<uint64_t>(ks * (2048 >> 4)), md.idesc_pv,
+                  (ks > 0 || !first) ? 1u : 0u);
+    }
+  }
 }
 
 __device__ void mma_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
                            int64_t g1) {
   volatile int* abort = &bars->abort;
-  const uint32_t idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, kBN, 0, 0);
-  const uint32_t idesc_pv = umma_idesc_f16(t.ab_fmt, kBM, kD, 0, 1);
-  const uint32_t q_base = smem_u32(smem + kOffQ);
-  const uint32_t kv_base = smem_u32(smem + kOffKV);
-  const uint32_t p_base = smem_u32(smem + kOffP);
-  int64_t i = 0;    // tiles consumed by this CTA
-  int seg = 0;
+  MmaDescs md;
+  {
+    const uint32_t q_base = smem_u32(smem + kOffQ);
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) md.q[mt][h] = umma_desc_sw128(q_base + (mt * 2 + h) * kQHalf, 16, 1024);
+    md.k0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+    md.v0 = umma_desc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
+    md.idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, kBN, 0, 0);
+    md.idesc_pv = umma_idesc_f16(t.ab_fmt, kBM, kD, 0, 1);
+  }
+  Ring kr, vr;          // K / V ring positions of the next Q.K^T / P.V
+  uint32_t i = 0;       // tiles consumed by this CTA
+  uint32_t seg = 0;
   bool ok = true;
-  auto issue_qk = [&](int64_t ti) {
-    const int stage = static_cast<int>(ti % kStages);
-    const uint32_t buf = static_cast<uint32_t>(ti & 1);
-    const uint32_t kst = kv_base + stage * kStageBytes;
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const uint32_t d_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
-#pragma unroll
-      for (int ks = 0; ks < kD / 16; ++ks) {
-        const uint32_t half = ks >> 2, off = (ks & 3) * 32;
-        const uint64_t a = umma_desc_sw128(q_base + (mt * 2 + half) * kQHalf + off, 16, 1024);
-        const uint64_t b = umma_desc_sw128(kst + half * kKVHalf + off, 16, 1024);
-        umma_f16_ss(d_tmem, a, b, idesc_qk, ks > 0 ? 1u : 0u);
-      }
-    }
-    umma_commit(&bars->s_full[buf]);
-  };
-  for (int64_t g = g0; g < g1 && ok;) {
+  for (int64_t g = g0; g < g1 && ok; ++seg) {
     const PairInfo pi = pair_info(t, pair_of(t, g));
-    const int64_t e = min(g1, pi.end);
-    if (!bounded_wait(&bars->q_full, static_cast<uint32_t>(seg) & 1u, abort)) { ok = false; break; }
-    tc_fence_after();
-    // first tile of the segment
-    if (!bounded_wait(&bars->kv_full[i % kStages], static_cast<uint32_t>(i / kStages) & 1u, abort)) {
+    const uint32_t n_tiles = static_cast<uint32_t>(min(g1, pi.end) - g);
+    if (!bounded_wait(&bars->q_full, seg & 1u, abort) || !bounded_wait(&bars->k_full[kr.stage], kr.phase, abort)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    issue_qk(i);
-    const int64_t i_first = i;
-    for (; g < e; ++g, ++i) {
-      if (g + 1 < e) {
-        const int64_t n = i + 1;
-        if (!bounded_wait(&bars->kv_full[n % kStages], static_cast<uint32_t>(n / kStages) & 1u, abort)) {
-          ok = false;
-          break;
+    issue_qk(md, tmem, kr.stage, i & 1u);
+    umma_commit(&bars->s_full[i & 1u]);
+    umma_commit(&bars->k_empty[kr.stage]);
+    kr.next();
+    for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
+      // Issue Q.K^T(i + 1) and P.V(i) in whichever order their inputs arrive,
+      // preferring Q.K^T so the next softmax can start early.
+      bool qk_done = j + 1 >= n_tiles;
+      bool pv_done = false, p_ok = false, v_ok = false;
+      const uint32_t buf = i & 1u;
+      long long t0 = 0;
+      uint32_t spins = 0;
+      while (!(qk_done && pv_done)) {
+        bool progress = false;
+        if (!qk_done && mbar_test_wait(&bars->k_full[kr.stage], kr.phase)) {
+          tc_fence_after();
+          issue_qk(md, tmem, kr.stage, buf ^ 1u);
+          umma_commit(&bars->s_full[buf ^ 1u]);
+          umma_commit(&bars->k_empty[kr.stage]);
+          kr.next();
+          qk_done = progress = true;
         }
-        tc_fence_after();
-        issue_qk(n);
-      }
-      const uint32_t buf = static_cast<uint32_t>(i & 1);
-      if (!bounded_wait(&bars->p_full[buf], static_cast<uint32_t>(i >> 1) & 1u, abort)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int stage = static_cast<int>(i % kStages);
-      const uint32_t vst = kv_base + stage * kStageBytes + 2 * kKVHalf;
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        const uint32_t d_tmem = tmem + kColO + mt * kD;
-        const uint32_t pa = p_base + (buf * 2 + mt) * kPTile;
-#pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint64_t a = umma_desc_sw128(pa + ks * 32, 16, 1024);
-          // V tile: MN-major (d contiguous); d halves 8 KB apart, 8-row groups 1 KB apart
-          const uint64_t b = umma_desc_sw128(vst + ks * 2048, kKVHalf, 1024);
-          umma_f16_ss(d_tmem, a, b, idesc_pv, (i > i_first || ks > 0) ? 1u : 0u);
+        if (!pv_done) {
+          p_ok = p_ok || mbar_test_wait(&bars->p_full[buf], (i >> 1) & 1u);
+          v_ok = v_ok || mbar_test_wait(&bars->v_full[vr.stage], vr.phase);
+          if (p_ok && v_ok) {
+            tc_fence_after();
+            issue_pv(md, tmem, vr.stage, buf, j == 0);
+            umma_commit(&bars->p_free[buf]);
+            umma_commit(&bars->v_empty[vr.stage]);
+            vr.next();
+            pv_done = progress = true;
+          }
+        }
+        if (!progress) {
+          ++spins;
+          if (spins == 1024) {
+            t0 = clock64();
+          } else if (spins > 1024 && (spins & 63u) == 0) {
+            if (*abort) { ok = false; break; }
+            if (clock64() - t0 > kWaitLimitCycles) { *abort = 1; ok = false; break; }
+          }
         }
       }
-      umma_commit(&bars->p_free[buf]);
-      umma_commit(&bars->kv_empty[stage]);
+      if (!ok) break;
+      g += 1;
     }
-    ++seg;
   }
   // all MMAs complete before TMEM is released
   umma_commit(&bars->drain);
@@ -293,6 +350,114 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+// Writes 32 finished output columns of one row (bf16 fast path or any dtype).
+__device__ __forceinline__ void store_cols32(const TcArgs& t, int64_t ob, int col0, const float (&v)[32]) {
+  if (t.out_vec) {
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.a.out) + ob + col0;
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) {
+      uint32_t w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat162 v2 = __floats2bfloat162_rn(v[c + 2 * u], v[c + 2 * u + 1]);
+        w[u] = *reinterpret_cast<const uint32_t*>(&v2);
+      }
+      *reinterpret_cast<uint4*>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) store_as(t.a.out, t.a.out_dtype, ob + col0 + c, v[c]);
+  }
+}
+
+// Merges the partials of one row of a pair that was cut between CTAs
+// first..last: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M).  All
+// loads of a 32-column chunk are issued before any is used.
+__device__ void combine_row(const TcArgs& t, int64_t first, int64_t last, int64_t pstart, int64_t T, int qrow,
+                            bool row_ok, int64_t ob, int64_t orow) {
+  constexpr int kMaxParts = 4;
+  const int parts = static_cast<int>(last - first + 1);
+  auto slot_of = [&](int64_t c) -> int64_t {
+    return c * 2 + ((c == first && pstart > range_start(c, T, t.grid)) ? 1 : 0);
+  };
+  float M = -INFINITY;
+  float lse_k[kMaxParts];
+  int64_t sl_k[kMaxParts];
+#pragma unroll
+  for (int k = 0; k < kMaxParts; ++k) {
+    sl_k[k] = k < parts ? slot_of(first + k) : 0;
+    lse_k[k] = k < parts ? __ldcg(t.part_lse + sl_k[k] * kQRows + qrow) : -INFINITY;
+  }
+  for (int64_t c = first + kMaxParts; c <= last; ++c) M = fmaxf(M, __ldcg(t.part_lse + slot_of(c) * kQRows + qrow));
+#pragma unroll
+  for (int k = 0; k < kMaxParts; ++k) M = fmaxf(M, lse_k[k]);
+  if (!row_ok) return;
+  const AttnArgs& a = t.a;
+  if (M == -INFINITY) {
+    for (int c = 0; c < kD; ++c) store_as(a.out, a.out_dtype, ob + c, NAN);
+    if (a.lse) a.lse[orow] = -INFINITY;
+    return;
+  }
+  float w_k[kMaxParts];
+  float wsum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxParts; ++k) {
+    w_k[k] = k < parts ? ex2_approx(lse_k[k] - M) : 0.f;
+    wsum += w_k[k];
+  }
+  for (int64_t c = first + kMaxParts; c <= last; ++c) wsum += ex2_approx(__ldcg(t.part_lse + slot_of(c) * kQRows + qrow) - M);
+  const float winv = 1.f / wsum;
+#pragma unroll 1
+  for (int ch = 0; ch < kD; ch += 64) {
+    float acc[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+    {
+      // the first two parts (the common case) with every load in flight
+      float4 v0[16], v1[16];
+      const float4* s0 = reinterpret_cast<const float4*>(t.part_o + (sl_k[0] * kQRows + qrow) * kD + ch);
+      const float4* s1 = reinterpret_cast<const float4*>(t.part_o + (sl_k[1] * kQRows + qrow) * kD + ch);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        v0[q] = __ldcg(s0 + q);
+        v1[q] = parts > 1 ? __ldcg(s1 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        acc[4 * q] = fmaf(w_k[0], v0[q].x, fmaf(w_k[1], v1[q].x, acc[4 * q]));
+        acc[4 * q + 1] = fmaf(w_k[0], v0[q].y, fmaf(w_k[1], v1[q].y, acc[4 * q + 1]));
+        acc[4 * q + 2] = fmaf(w_k[0], v0[q].z, fmaf(w_k[1], v1[q].z, acc[4 * q + 2]));
+        acc[4 * q + 3] = fmaf(w_k[0], v0[q].w, fmaf(w_k[1], v1[q].w, acc[4 * q + 3]));
+      }
+    }
+    for (int64_t c = first + 2; c <= last; ++c) {
+      const int64_t sl = c - first < kMaxParts ? sl_k[c - first] : slot_of(c);
+      const float w = c - first < kMaxParts ? w_k[c - first]
+                                            : ex2_approx(__ldcg(t.part_lse + sl * kQRows + qrow) - M);
+      const float4* src = reinterpret_cast<const float4*>(t.part_o + (sl * kQRows + qrow) * kD + ch);
+      float4 v[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) v[q] = __ldcg(src + q);
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        acc[4 * q] = fmaf(w, v[q].x, acc[4 * q]);
+        acc[4 * q + 1] = fmaf(w, v[q].y, acc[4 * q + 1]);
+        acc[4 * q + 2] = fmaf(w, v[q].z, acc[4 * q + 2]);
+        acc[4 * q + 3] = fmaf(w, v[q].w, acc[4 * q + 3]);
+      }
+    }
+    float lo[32], hi[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      lo[c] = acc[c] * winv;
+      hi[c] = acc[32 + c] * winv;
+    }
+    store_cols32(t, ob, ch, lo);
+    store_cols32(t, ob, ch + 32, hi);
+  }
+  if (a.lse) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+}
+
 template <int ANCW>
 __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
                                  int64_t g1, int64_t T, int cta) {
@@ -307,6 +472,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
   uint8_t* q_tile = smem + kOffQ + wg * 2 * kQHalf;
   const int R = a.group * a.n;
   const float sl2 = a.scale_log2;
+  const bool ab_bf16 = t.ab_fmt != 0;
   const int qrow = wg * kBM + r;                // row within the pair's 256
   int64_t i = 0;
   for (int64_t g = g0; g < g1;) {
@@ -341,30 +507,46 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     uint32_t anc[ANCW];
 #pragma unroll
     for (int k = 0; k < ANCW; ++k) anc[k] = 0;
-    if (row_ok && len_ok) {
-      if (a.mask_kind == GORGON_MASK_PARENTS) {
-        const int32_t* par = a.parents + static_cast<int64_t>(pi.b) * a.par_sb;
-        int cur = node;
-        for (int hop = -1; hop < a.max_depth && cur >= 0; ++hop) {
-          if (cur >= a.n) {
-            raise_device_error(a.err, kErrBadParent);
-            break;
-          }
+    if (a.mask_kind == GORGON_MASK_PARENTS) {
+      // The warp keeps parents[] in registers (lane l holds entries l, l + 32,
+      // ...) and every lane walks its own node's chain through shuffles, so
+      // the walk costs one coalesced load instead of a chain of dependent ones.
+      const int32_t* par = a.parents + static_cast<int64_t>(pi.b) * a.par_sb;
+      int pv[ANCW];
+#pragma unroll
+      for (int k = 0; k < ANCW; ++k) {
+        const int idx = lane + 32 * k;
+        pv[k] = (len_ok && idx < a.n) ? par[idx] : -1;
+      }
+      int cur = (row_ok && len_ok) ? node : -1;
+      bool bad = false;
+      for (int hop = -1; hop < a.max_depth; ++hop) {
+        if (!__any_sync(0xffffffffu, cur >= 0)) break;
+        if (cur >= a.n) {
+          bad = true;
+          cur = -1;
+        }
+#pragma unroll
+        for (int k = 0; k < ANCW; ++k)
+          if (cur >= 0 && (cur >> 5) == k) anc[k] |= 1u << (cur & 31);
+        int nxt = -1;
+#pragma unroll
+        for (int k = 0; k < ANCW; ++k) {
+          const int v = __shfl_sync(0xffffffffu, pv[k], cur & 31);
+          if ((cur >> 5) == k) nxt = v;
+        }
+        cur = cur >= 0 ? nxt : -1;
+      }
+      if (bad) raise_device_error(a.err, kErrBadParent);
+    } else if (row_ok && len_ok) {
+      const uint8_t* mrow =
+          a.mask + static_cast<int64_t>(pi.b) * a.mask_sb + static_cast<int64_t>(node) * a.mask_sn;
+      for (int j = 0; j < a.n; ++j)
+        if (mrow[j]) {
 #pragma unroll
           for (int k = 0; k < ANCW; ++k)
-            if ((cur >> 5) == k) anc[k] |= 1u << (cur & 31);
-          cur = par[cur];
+            if ((j >> 5) == k) anc[k] |= 1u << (j & 31);
         }
-      } else {
-        const uint8_t* mrow =
-            a.mask + static_cast<int64_t>(pi.b) * a.mask_sb + static_cast<int64_t>(node) * a.mask_sn;
-        for (int j = 0; j < a.n; ++j)
-          if (mrow[j]) {
-#pragma unroll
-            for (int k = 0; k < ANCW; ++k)
-              if ((j >> 5) == k) anc[k] |= 1u << (j & 31);
-          }
-      }
     }
     if (!len_ok && qrow == 0) raise_device_error(a.err, kErrBadSeqlen);
 
@@ -387,23 +569,23 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
         }
       }
       const int c0 = static_cast<int>(g - pi.start) * kBN;
-      float tmax = -INFINITY;
+      // row max of the raw scores (scale > 0, so it commutes with max)
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (len_ok && c0 + kBN <= P) {
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          x[c] *= sl2;
-          tmax = fmaxf(tmax, x[c]);
-        }
+        for (int c = 0; c < kBN; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], x[c], x[c + 1]);
       } else {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
           const int col = c0 + c;
           const int tt = col - P;
           const bool vis = len_ok && col < pi.L && (tt < 0 || anc_bit<ANCW>(anc, tt));
-          x[c] = vis ? x[c] * sl2 : -INFINITY;
-          tmax = fmaxf(tmax, x[c]);
+          x[c] = vis ? x[c] : -INFINITY;
         }
+#pragma unroll
+        for (int c = 0; c < kBN; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], x[c], x[c + 1]);
       }
+      const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
       // lazy running max: move it only when this tile exceeds it by > 8
       float alpha = 1.f;
       bool need = false;
@@ -414,15 +596,19 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
         m_used = tmax;
         need = true;
       }
-      const float mb = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
+      const float nmb = m_used == -INFINITY ? 0.f : -m_used;
+      const uint64_t sl2_2 = f2_pack(sl2, sl2), nmb_2 = f2_pack(nmb, nmb);
+      uint64_t acc2[4] = {0, 0, 0, 0};  // bit pattern of (0.f, 0.f)
       uint32_t packed[kBN / 2];
 #pragma unroll
       for (int c = 0; c < kBN; c += 2) {
-        const float p0 = ex2_approx(x[c] - mb);
-        const float p1 = ex2_approx(x[c + 1] - mb);
-        sum += p0 + p1;
-        if (t.ab_fmt) {
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(x[c], x[c + 1]), sl2_2, nmb_2), a0, a1);
+        const float p0 = ex2_approx(a0);
+        const float p1 = ex2_approx(a1);
+        const uint64_t pp = f2_pack(p0, p1);
+        acc2[(c >> 1) & 3] = f2_add(acc2[(c >> 1) & 3], pp);
+        if (ab_bf16) {
           const __nv_bfloat162 v2 = __floats2bfloat162_rn(p0, p1);
           packed[c >> 1] = *reinterpret_cast<const uint32_t*>(&v2);
         } else {
@@ -430,9 +616,14 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
           packed[c >> 1] = *reinterpret_cast<const uint32_t*>(&v2);
         }
       }
+      float sum;
+      {
+        const uint64_t s2 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
+        float s0, s1;
+        f2_unpack(s2, s0, s1);
+        sum = s0 + s1;
+      }
       l = l * alpha + sum;
-      // this P buffer was last read by the P.V MMA of tile i - 2
-      if (i >= 2 && !warp_wait(&bars->p_free[buf], static_cast<uint32_t>((i - 2) >> 1) & 1u, abort)) return;
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
@@ -450,14 +641,9 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
         }
         tmem_wait_st();
       }
-      // P row -> shared memory (SW128 K-major, 64 columns = one 128-byte row)
-      uint8_t* pt = smem + kOffP + (buf * 2 + wg) * kPTile;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(pt + sw128(r, c)) =
-            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-      }
-      fence_proxy_async_smem();
+      // P row (bf16 pairs) -> the first 32 columns of this tile's S buffer
+      tmem_st32(lane_base + kColS + (buf * 2 + wg) * kBN, packed);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[buf]);
@@ -480,26 +666,10 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
         uint32_t ov[32];
         tmem_ld32(o_addr + ch * 32, ov);
         tmem_wait_ld();
-        if (row_ok) {
-          if (t.out_vec) {
-            __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(a.out) + ob + ch * 32;
+        float vals[32];
 #pragma unroll
-            for (int c = 0; c < 32; c += 8) {
-              uint32_t w[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const __nv_bfloat162 v2 = __floats2bfloat162_rn(__uint_as_float(ov[c + 2 * u]) * inv,
-                                                                __uint_as_float(ov[c + 2 * u + 1]) * inv);
-                w[u] = *reinterpret_cast<const uint32_t*>(&v2);
-              }
-              *reinterpret_cast<uint4*>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 32; ++c)
-              store_as(a.out, a.out_dtype, ob + ch * 32 + c, __uint_as_float(ov[c]) * inv);
-          }
-        }
+        for (int c = 0; c < 32; ++c) vals[c] = __uint_as_float(ov[c]) * inv;
+        if (row_ok) store_cols32(t, ob, ch * 32, vals);
       }
       if (row_ok && a.lse) a.lse[orow] = lse2 * 0.6931471805599453f;
       continue;
@@ -521,61 +691,29 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
                         any ? __uint_as_float(ov[c + 2]) * inv : 0.f, any ? __uint_as_float(ov[c + 3]) * inv : 0.f);
     }
     t.part_lse[slot * kQRows + qrow] = lse2;
-    __threadfence();
+    // per-warp arrival count: the warp that completes the set of parts merges
+    // them.  The warp barrier orders every lane's stores before lane 0's
+    // release atomic; the merging warp acquires before reading the others'.
     __syncwarp();
-    // per-warp arrival count: the warp that completes the set of parts merges them
     const int64_t first = cta_of(pi.start, T, t.grid);
     const int64_t last = cta_of(pi.end - 1, T, t.grid);
     int is_last = 0;
     if (lane == 0) {
-      const int prev = atomicAdd(t.counters + static_cast<int64_t>(p) * 8 + wslot, 1);
+      __threadfence();
+      const int prev = atomic_add_release_gpu(t.counters + static_cast<int64_t>(p) * 8 + wslot, 1);
       is_last = prev == static_cast<int>(last - first);
     }
     is_last = __shfl_sync(0xffffffffu, is_last, 0);
     if (!is_last) continue;
-    __threadfence();
-    float M = -INFINITY;
-    for (int64_t c = first; c <= last; ++c) {
-      const int wh = (c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0;
-      M = fmaxf(M, __ldcg(t.part_lse + (c * 2 + wh) * kQRows + qrow));
-    }
-    if (!row_ok) continue;
-    if (M == -INFINITY) {
-      for (int c = 0; c < kD; ++c) store_as(a.out, a.out_dtype, ob + c, NAN);
-      if (a.lse) a.lse[orow] = -INFINITY;
-      continue;
-    }
-    float wsum = 0.f;
-    for (int64_t c = first; c <= last; ++c) {
-      const int wh = (c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0;
-      wsum += ex2_approx(__ldcg(t.part_lse + (c * 2 + wh) * kQRows + qrow) - M);
-    }
-    const float winv = 1.f / wsum;
-    for (int ch = 0; ch < kD; ch += 4) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int64_t c = first; c <= last; ++c) {
-        const int wh = (c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0;
-        const int64_t sl = c * 2 + wh;
-        const float w = ex2_approx(__ldcg(t.part_lse + sl * kQRows + qrow) - M);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(t.part_o + (sl * kQRows + qrow) * kD + ch));
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
-      store_as(a.out, a.out_dtype, ob + ch, acc.x * winv);
-      store_as(a.out, a.out_dtype, ob + ch + 1, acc.y * winv);
-      store_as(a.out, a.out_dtype, ob + ch + 2, acc.z * winv);
-      store_as(a.out, a.out_dtype, ob + ch + 3, acc.w * winv);
-    }
-    if (a.lse) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+    fence_acquire_gpu();
+    combine_row(t, first, last, pi.start, T, qrow, row_ok, ob, orow);
   }
 }
 
 template <int ANCW>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-               const TcArgs t) {
+               const __grid_constant__ TcArgs t) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
@@ -584,8 +722,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->k_full[s], 1);
+      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->v_full[s], 1);
+      mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->q_full, 8);
     for (int b = 0; b < 2; ++b) {
@@ -617,13 +757,16 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 
   if (g0 < g1) {
     if (warp == 0) {
-      if (lane == 0) producer(t, &kmap, &vmap, smem, bars, g0, g1);
+      if (lane == 0) producer(t, &kmap, smem, bars, g0, g1, 0);
+    } else if (warp == 3) {
+      if (lane == 0) producer(t, &vmap, smem, bars, g0, g1, 1);
     } else if (warp == 1) {
       if (lane == 0) mma_issuer(t, smem, bars, tmem, g0, g1);
     } else if (warp >= 4) {
       softmax_epilogue<ANCW>(t, smem, bars, tmem, g0, g1, T, blockIdx.x);
     }
   }
+  __syncwarp();  // role warps ran their loop on lane 0: reconverge before the CTA barrier
   tc_fence_before();
   __syncthreads();
   if (bars->abort && threadIdx.x == 0) raise_device_error(t.a.err, kErrTimeout);

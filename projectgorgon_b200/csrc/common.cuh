@@ -9,7 +9,7 @@
 #include <cmath>
 #include <string>
 
-#include "../../include/gorgon_b200.h"
+#include "gorgon_b200.h"
 
 namespace gorgon {
 
