@@ -42,7 +42,10 @@ from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
-NCU_TRAFFIC_BYTES = {}
+NCU_TRAFFIC_BYTES = {
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.55 MB read + 3.50 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 553047552,
+}
 
 WORKLOADS = {
     "verify-b16-p8192-n64": dict(B=16, Hq=32, Hkv=8, D=128, P=8192, N=64, dtype="bf16",

@@ -127,7 +127,8 @@ typedef struct {
   float scale;
   float* lse;                     /* nullable */
   int32_t backend;                /* gorgon_backend */
-  int32_t num_splits;             /* CUDA-core kernel splits; 0 = chosen by the library */
+  int32_t num_splits;             /* key/value splits (CUDA-core kernel) or CTAs
+                                     (tcgen05 kernel); 0 = chosen by the library */
   int64_t kv_rows;                /* with cu_seqlens: rows of k and v (0 = unknown, which
                                      keeps ragged batches on the CUDA-core kernel) */
 } gorgon_tree_attn_params;

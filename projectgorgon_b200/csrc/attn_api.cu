@@ -75,6 +75,7 @@ int make_args(const gorgon_tree_attn_params* p, AttnArgs* a) {
   x.mask_kind = p->mask_kind;
   x.max_depth = p->max_depth < 0 ? x.n : p->max_depth;
   x.out_dtype = p->out_dtype;
+  x.splits = p->num_splits;  // tensor-core grid request; the CUDA-core path sets its own
   const float scale = p->scale != 0.f ? p->scale : (x.d > 0 ? 1.f / std::sqrt(static_cast<float>(x.d)) : 1.f);
   x.scale_log2 = scale * 1.4426950408889634f;
   const int ev = static_cast<int>(16 / dtype_bytes(p->dtype));

@@ -5,8 +5,9 @@
 // g * n + i.  Those rows share every key/value row of the pair, so each K/V
 // tile is fetched from HBM once and used by two 128-row MMA tiles.
 //
-// Schedule: a persistent grid (at most one CTA per SM) splits the global list
-// of 64-row key/value tiles, pair-major, into equal contiguous ranges.  A pair
+// Schedule: a grid of at most one CTA per SM.  When pairs roughly fill the
+// SMs, each CTA takes whole pairs.  Otherwise (stream-K) the pair-major list
+// of 64-row key/value tiles is split into equal contiguous ranges: a pair
 // that falls inside one CTA is finished there; a pair cut between CTAs leaves
 // normalised partials plus log-sum-exp in the workspace and the CTA that
 // finishes it last merges them (no spinning: an atomic arrival count).
@@ -14,9 +15,9 @@
 // Warp roles (384 threads):
 //   warp 0       TMA producer for K tiles (two 64-column SW128 boxes), 5-stage ring
 //   warp 3       TMA producer for V tiles, its own 5-stage ring
-//   warp 1       MMA issuer (one thread): S = Q K^T into TMEM, O += P V with P
-//                read from TMEM; it never holds P.V(i) back behind K(i + 1)
-//   warp 2       TMEM allocation / release
+//   warp 1       Q.K^T issuer (one thread): S = Q K^T into TMEM
+//   warp 2       P.V issuer (one thread): O += P V with P read from TMEM; the
+//                warp also allocates and releases TMEM
 //   warps 4-7    softmax + epilogue of M-tile 0 (TMEM lanes 0-127)
 //   warps 8-11   softmax + epilogue of M-tile 1
 // TMEM (512 columns): S double-buffered (2 buffers x 2 M-tiles x 64 columns),
@@ -74,6 +75,7 @@ struct TcArgs {
   int pairs;          // batch * hkv * qgroups
   int tiles_per_pair; // uniform lengths only
   int grid;
+  int pair_align;     // CTA ranges hold whole pairs (no partials to merge)
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // bf16 output with 16-byte aligned rows
   int* counters;      // [pairs][8] arrivals of partial pairs, per softmax warp
@@ -91,7 +93,7 @@ struct Barriers {
   uint64_t s_full[2];
   uint64_t p_full[2];
   uint64_t p_free[2];  // P.V of the tile in this buffer has completed
-  uint64_t drain;
+  uint64_t drain[2];   // all MMAs of the Q.K^T / P.V issuer complete
   uint32_t tmem_base;
   int abort;
 };
@@ -152,6 +154,27 @@ __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
 
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   return mbar_wait(bar, parity, abort, kWaitLimitCycles);
+}
+
+// Wait of a thread that does nothing else (the MMA issuers): spins on the
+// non-blocking test so it resumes the moment the phase completes, instead of
+// sleeping in try_wait.  Bounded like bounded_wait.
+__device__ __forceinline__ bool spin_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test_wait(bar, parity)) return true;
+  long long t0 = 0;
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      const long long now = clock64();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitCycles) {
+        *abort = 1;
+        return false;
+      }
+    }
+  }
 }
 
 // Wait used on the way out: ignores the abort flag, gives up after about 100 ms.
@@ -255,84 +278,81 @@ __device__ __forceinline__ void issue_pv(const MmaDescs& md, uint32_t tmem, uint
   }
 }
 
-__device__ void mma_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
-                           int64_t g1) {
+__device__ __forceinline__ void make_descs(const TcArgs& t, uint8_t* smem, MmaDescs& md) {
+  const uint32_t q_base = smem_u32(smem + kOffQ);
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) md.q[mt][h] = umma_desc_sw128(q_base + (mt * 2 + h) * kQHalf, 16, 1024);
+  md.k0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+  md.v0 = umma_desc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
+  md.idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, kBN, 0, 0);
+  md.idesc_pv = umma_idesc_f16(t.ab_fmt, kBM, kD, 0, 1);
+}
+
+// Two threads (in different warps) feed the tensor pipe: one issues every
+// Q.K^T, the other every P.V, so neither group waits behind the other's
+// bookkeeping.  S buffer i & 1 doubles as P's storage, so Q.K^T(i) waits for
+// P.V(i - 2) to complete before overwriting it.  Both spin on their barriers
+// (they have nothing else to do) to start the moment their inputs land.
+__device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0, int64_t g1) {
   volatile int* abort = &bars->abort;
   MmaDescs md;
-  {
-    const uint32_t q_base = smem_u32(smem + kOffQ);
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) md.q[mt][h] = umma_desc_sw128(q_base + (mt * 2 + h) * kQHalf, 16, 1024);
-    md.k0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
-    md.v0 = umma_desc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
-    md.idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, kBN, 0, 0);
-    md.idesc_pv = umma_idesc_f16(t.ab_fmt, kBM, kD, 0, 1);
-  }
-  Ring kr, vr;          // K / V ring positions of the next Q.K^T / P.V
-  uint32_t i = 0;       // tiles consumed by this CTA
-  uint32_t seg = 0;
-  bool ok = true;
-  for (int64_t g = g0; g < g1 && ok; ++seg) {
+  make_descs(t, smem, md);
+  Ring kr;
+  uint32_t i = 0, seg = 0;
+  for (int64_t g = g0; g < g1; ++seg) {
     const PairInfo pi = pair_info(t, pair_of(t, g));
     const uint32_t n_tiles = static_cast<uint32_t>(min(g1, pi.end) - g);
-    if (!bounded_wait(&bars->q_full, seg & 1u, abort) || !bounded_wait(&bars->k_full[kr.stage], kr.phase, abort)) {
-      ok = false;
-      break;
-    }
-    tc_fence_after();
-    issue_qk(md, tmem, kr.stage, i & 1u);
-    umma_commit(&bars->s_full[i & 1u]);
-    umma_commit(&bars->k_empty[kr.stage]);
-    kr.next();
+    if (!spin_wait(&bars->q_full, seg & 1u, abort)) break;
+    bool ok = true;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
-      // Issue Q.K^T(i + 1) and P.V(i) in whichever order their inputs arrive,
-      // preferring Q.K^T so the next softmax can start early.
-      bool qk_done = j + 1 >= n_tiles;
-      bool pv_done = false, p_ok = false, v_ok = false;
-      const uint32_t buf = i & 1u;
-      long long t0 = 0;
-      uint32_t spins = 0;
-      while (!(qk_done && pv_done)) {
-        bool progress = false;
-        if (!qk_done && mbar_test_wait(&bars->k_full[kr.stage], kr.phase)) {
-          tc_fence_after();
-          issue_qk(md, tmem, kr.stage, buf ^ 1u);
-          umma_commit(&bars->s_full[buf ^ 1u]);
-          umma_commit(&bars->k_empty[kr.stage]);
-          kr.next();
-          qk_done = progress = true;
-        }
-        if (!pv_done) {
-          p_ok = p_ok || mbar_test_wait(&bars->p_full[buf], (i >> 1) & 1u);
-          v_ok = v_ok || mbar_test_wait(&bars->v_full[vr.stage], vr.phase);
-          if (p_ok && v_ok) {
-            tc_fence_after();
-            issue_pv(md, tmem, vr.stage, buf, j == 0);
-            umma_commit(&bars->p_free[buf]);
-            umma_commit(&bars->v_empty[vr.stage]);
-            vr.next();
-            pv_done = progress = true;
-          }
-        }
-        if (!progress) {
-          ++spins;
-          if (spins == 1024) {
-            t0 = clock64();
-          } else if (spins > 1024 && (spins & 63u) == 0) {
-            if (*abort) { ok = false; break; }
-            if (clock64() - t0 > kWaitLimitCycles) { *abort = 1; ok = false; break; }
-          }
-        }
+      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort) ||
+          (i >= 2 && !spin_wait(&bars->p_free[i & 1u], ((i - 2) >> 1) & 1u, abort))) {
+        ok = false;
+        break;
       }
-      if (!ok) break;
-      g += 1;
+      tc_fence_after();
+      issue_qk(md, tmem, kr.stage, i & 1u);
+      umma_commit(&bars->s_full[i & 1u]);
+      umma_commit(&bars->k_empty[kr.stage]);
+      kr.next();
     }
+    if (!ok) break;
+    g += n_tiles;
   }
-  // all MMAs complete before TMEM is released
-  umma_commit(&bars->drain);
-  drain_wait(&bars->drain, 0);
+  umma_commit(&bars->drain[0]);
+  drain_wait(&bars->drain[0], 0);
+}
+
+__device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0, int64_t g1) {
+  volatile int* abort = &bars->abort;
+  MmaDescs md;
+  make_descs(t, smem, md);
+  Ring vr;
+  uint32_t i = 0;
+  for (int64_t g = g0; g < g1;) {
+    const PairInfo pi = pair_info(t, pair_of(t, g));
+    const uint32_t n_tiles = static_cast<uint32_t>(min(g1, pi.end) - g);
+    bool ok = true;
+    for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
+      const uint32_t buf = i & 1u;
+      if (!spin_wait(&bars->p_full[buf], (i >> 1) & 1u, abort) ||
+          !spin_wait(&bars->v_full[vr.stage], vr.phase, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      issue_pv(md, tmem, vr.stage, buf, j == 0);
+      umma_commit(&bars->p_free[buf]);
+      umma_commit(&bars->v_empty[vr.stage]);
+      vr.next();
+    }
+    if (!ok) break;
+    g += n_tiles;
+  }
+  umma_commit(&bars->drain[1]);
+  drain_wait(&bars->drain[1], 0);
 }
 
 template <int ANCW>
@@ -733,7 +753,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       mbar_init(&bars->p_full[b], 8);
       mbar_init(&bars->p_free[b], 1);
     }
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain[0], 1);
+    mbar_init(&bars->drain[1], 1);
     bars->abort = 0;
     fence_barrier_init();
   }
@@ -752,8 +773,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 
   const int64_t T = total_tiles(t);
   const int64_t G = t.grid;
-  const int64_t g0 = range_start(blockIdx.x, T, G);
-  const int64_t g1 = range_start(blockIdx.x + 1, T, G);
+  int64_t g0, g1;
+  if (t.pair_align) {
+    g0 = pair_start(t, static_cast<int>(static_cast<int64_t>(blockIdx.x) * t.pairs / G));
+    g1 = pair_start(t, static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * t.pairs / G));
+  } else {
+    g0 = range_start(blockIdx.x, T, G);
+    g1 = range_start(blockIdx.x + 1, T, G);
+  }
 
   if (g0 < g1) {
     if (warp == 0) {
@@ -761,7 +788,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     } else if (warp == 3) {
       if (lane == 0) producer(t, &vmap, smem, bars, g0, g1, 1);
     } else if (warp == 1) {
-      if (lane == 0) mma_issuer(t, smem, bars, tmem, g0, g1);
+      if (lane == 0) qk_issuer(t, smem, bars, tmem, g0, g1);
+    } else if (warp == 2) {
+      if (lane == 0) pv_issuer(t, smem, bars, tmem, g0, g1);
     } else if (warp >= 4) {
       softmax_epilogue<ANCW>(t, smem, bars, tmem, g0, g1, T, blockIdx.x);
     }
@@ -812,7 +841,7 @@ EncodeTiledFn encode_fn() {
 
 struct Plan {
   int qgroups, pairs, tiles_per_pair, grid;
-  bool varlen;
+  bool varlen, pair_align;
 };
 
 Plan make_plan(const AttnArgs& a) {
@@ -822,14 +851,30 @@ Plan make_plan(const AttnArgs& a) {
   pl.pairs = a.batch * a.hkv * pl.qgroups;
   pl.varlen = a.cu_seqlens != nullptr;
   const int sms = sm_count();
+  pl.pair_align = false;
   if (pl.varlen) {
     pl.tiles_per_pair = 0;
-    pl.grid = sms;
+    pl.grid = a.splits > 0 ? a.splits : sms;
   } else {
     pl.tiles_per_pair = (a.kv_len + kBN - 1) / kBN;
     const int64_t T = static_cast<int64_t>(pl.pairs) * pl.tiles_per_pair;
-    // at least 4 tiles per CTA so partials stay a small share of the work
-    pl.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, (T + 3) / 4)));
+    if (a.splits > 0) {
+      pl.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.splits, T)));
+    } else {
+      // Whole pairs per CTA avoid the partial write, the arrival atomics and
+      // the merge, which cost about a fifth of a pair's time on a loaded GPU
+      // (measured on the 16 x 8192-row Llama-3-8B layer); take them unless
+      // stream-K's even split is more than that much shorter.
+      const int64_t per_cta = (pl.pairs + sms - 1) / sms;
+      const int64_t cost_pairs = per_cta * pl.tiles_per_pair;
+      if (cost_pairs * 5 <= ((T + sms - 1) / sms) * 6) {
+        pl.pair_align = true;
+        pl.grid = static_cast<int>((pl.pairs + per_cta - 1) / per_cta);
+      } else {
+        // at least 4 tiles per CTA so partials stay a small share of the work
+        pl.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, (T + 3) / 4)));
+      }
+    }
   }
   return pl;
 }
@@ -917,6 +962,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.pairs = pl.pairs;
   t.tiles_per_pair = pl.tiles_per_pair;
   t.grid = pl.grid;
+  t.pair_align = pl.pair_align;
   t.ab_fmt = dtype == GORGON_BF16 ? 1 : 0;
   char* ws = static_cast<char*>(workspace);
   t.counters = reinterpret_cast<int*>(ws + w.counters);

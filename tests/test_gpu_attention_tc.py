@@ -139,3 +139,16 @@ def test_auto_picks_tensor_cores_for_64_node_trees():
     assert G.tree_attention_plan(q, k, v, parents=par)["backend"] == "tcgen05"
     q2, k2, v2 = _inputs(1, 32, 8, 31, 512)
     assert G.tree_attention_plan(q2, k2, v2, parents=_trees(1, 31, 0)[0])["backend"] == "simt"
+
+
+@pytest.mark.parametrize("grid", [1, 7, 16, 33])
+def test_tc_explicit_grid_sizes(grid):
+    """num_splits sets the tcgen05 grid: one CTA per pair (16), pairs cut
+    between CTAs (7, 33) and a single CTA walking every pair (1)."""
+    B, N, P = 2, 64, 700
+    pars = torch.tensor(_trees(B, N, seed=grid), device="cuda")
+    q, k, v = _inputs(B, 32, 8, N, P + N, seed=grid)
+    a = G.fused_tree_verify(q, k, v, pars, max_depth=5, backend="tcgen05", num_splits=grid)
+    assert G.tree_attention_plan(q, k, v, parents=pars, backend="tcgen05", num_splits=grid)["splits"] == grid
+    b = G.fused_tree_verify(q, k, v, pars, max_depth=5, backend="simt")
+    torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
