@@ -37,6 +37,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 import projectgorgon_b200 as G  # noqa: E402
+from projectgorgon_b200 import sharding  # noqa: E402
 from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
@@ -69,43 +70,52 @@ def log(*a):
 # workload construction
 # --------------------------------------------------------------------------
 class Workload:
-    """Seeded synthetic inputs of one workload, resident on `dev`."""
+    """Seeded synthetic inputs of one workload, resident on `dev`.
 
-    def __init__(self, name: str, dev: torch.device, seed: int):
+    Sequence j of this rank is global sequence first_seq + j, and everything
+    about it (prefix length, tree, q/k/v) comes from generators seeded by that
+    global index, so the union of all ranks' shards is one well-defined job
+    whatever the number of ranks."""
+
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
         cfg = WORKLOADS[name]
         self.name, self.cfg, self.dev = name, cfg, dev
         B, Hq, Hkv, D, N = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"]
-        rng = random.Random(seed)
-        if isinstance(cfg["P"], tuple):
-            self.prefixes = [rng.randint(*cfg["P"]) for _ in range(B)]
-        else:
-            self.prefixes = [cfg["P"]] * B
         self.ragged = isinstance(cfg["P"], tuple)
+        rngs = [random.Random(1_000_003 + first_seq + j) for j in range(B)]
+        self.prefixes = [r.randint(*cfg["P"]) if self.ragged else cfg["P"] for r in rngs]
         if cfg["tree"] == "random":
-            self.parents = [random_tree(N, rng, cfg["max_depth"]) for _ in range(B)]
+            self.parents = [random_tree(N, r, cfg["max_depth"]) for r in rngs]
         else:
             self.parents = [cartesian_tree(4, 2, True)] * B
         self.max_depth = cfg["max_depth"]
         dt = TORCH_DT[cfg["dtype"]]
         self.dtype = dt
-        g = torch.Generator(device=dev).manual_seed(seed)
         s = 1.0 / math.sqrt(D)
-        self.q = (torch.randn(B, Hq, N, D, device=dev, generator=g) * s).to(dt)
+        gens = [torch.Generator(device=dev).manual_seed(first_seq + j) for j in range(B)]
+        self.q = torch.empty(B, Hq, N, D, device=dev, dtype=dt)
+        for j in range(B):
+            self.q[j] = (torch.randn(Hq, N, D, device=dev, generator=gens[j]) * s).to(dt)
+        lens = [p + N for p in self.prefixes]
         if self.ragged:
-            lens = [p + N for p in self.prefixes]
             self.cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=dev)
             total = int(sum(lens))
-            self.k = (torch.randn(total, Hkv, D, device=dev, generator=g) * s).to(dt)
-            self.v = (torch.randn(total, Hkv, D, device=dev, generator=g) * s).to(dt)
+            self.k = torch.empty(total, Hkv, D, device=dev, dtype=dt)
+            self.v = torch.empty(total, Hkv, D, device=dev, dtype=dt)
+            off = 0
+            for j, L in enumerate(lens):
+                self.k[off:off + L] = (torch.randn(L, Hkv, D, device=dev, generator=gens[j]) * s).to(dt)
+                self.v[off:off + L] = (torch.randn(L, Hkv, D, device=dev, generator=gens[j]) * s).to(dt)
+                off += L
             self.max_seqlen = max(lens)
         else:
-            L = self.prefixes[0] + N
+            L = lens[0]
             self.cu = None
             self.k = torch.empty(B, Hkv, L, D, device=dev, dtype=dt)
             self.v = torch.empty(B, Hkv, L, D, device=dev, dtype=dt)
-            for b in range(B):  # per-sequence fill keeps the fp32 temporary small
-                self.k[b] = (torch.randn(Hkv, L, D, device=dev, generator=g) * s).to(dt)
-                self.v[b] = (torch.randn(Hkv, L, D, device=dev, generator=g) * s).to(dt)
+            for j in range(B):  # per-sequence fill keeps the fp32 temporary small
+                self.k[j] = (torch.randn(Hkv, L, D, device=dev, generator=gens[j]) * s).to(dt)
+                self.v[j] = (torch.randn(Hkv, L, D, device=dev, generator=gens[j]) * s).to(dt)
             self.max_seqlen = L
         self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
         esz = torch.tensor([], dtype=dt).element_size()
@@ -268,10 +278,8 @@ def cpu_baseline(wl: "Workload", budget_s: float = 12.0, max_slices: int = 64):
 # timing
 # --------------------------------------------------------------------------
 def dist_setup():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    env = sharding.dist_env()
+    return env.world, env.rank, env.local_rank
 
 
 def time_device(wl: Workload, steps: int, warmup: int, world: int):
@@ -355,11 +363,7 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
 
 
 def max_over_ranks(x: float, world: int, dev) -> float:
-    if world == 1:
-        return x
-    t = torch.tensor([x], dtype=torch.float64, device=dev)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
+    return sharding.max_over_ranks(x, dev) if world > 1 else x
 
 
 def peaks():
@@ -376,12 +380,10 @@ def run_ours(args):
         raise SystemExit("bench.py needs a CUDA device")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
+    sharding.init(sharding.dist_env(), "nccl", dev, timeout_s=120)
     G.load_library()
-    wl = Workload(args.workload, dev, seed=1000 * rank)
+    # weak scaling by sequence: rank r verifies global sequences [r*B, (r+1)*B)
+    wl = Workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
     plan = wl.plan()
     total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
     total_ms = max_over_ranks(total_ms, world, dev)
