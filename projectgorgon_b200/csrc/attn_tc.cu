@@ -61,7 +61,7 @@ constexpr uint32_t kOffQ = 0;                          // [mtile][half]
 constexpr uint32_t kOffK = kOffQ + 4 * kQHalf;         // [stage][half]
 constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
 constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + alignment slack
+constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;  // + alignment slack
 
 // TMEM columns
 constexpr uint32_t kTmemCols = 512;
@@ -90,14 +90,15 @@ struct Barriers {
   uint64_t v_full[kStages];
   uint64_t v_empty[kStages];
   uint64_t q_full;
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t p_free[2];  // P.V of the tile in this buffer has completed
+  // per (S buffer, M-tile): index buf * 2 + mtile
+  uint64_t s_full[4];
+  uint64_t p_full[4];
+  uint64_t p_free[4];  // P.V of the tile in this buffer has completed
   uint64_t drain[2];   // all MMAs of the Q.K^T / P.V issuer complete
   uint32_t tmem_base;
   int abort;
 };
-static_assert(sizeof(Barriers) <= 256, "barrier block");
+static_assert(sizeof(Barriers) <= 512, "barrier block");
 
 // ------------------------------------------------------------ schedule
 __device__ __forceinline__ int64_t total_tiles(const TcArgs& t) {
@@ -247,34 +248,28 @@ struct MmaDescs {
   uint32_t idesc_qk, idesc_pv;
 };
 
-// S = Q K^T of one tile into S buffer `buf`, both M-tiles.
-__device__ __forceinline__ void issue_qk(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf) {
+// S_mt = Q_mt K^T of one tile into S buffer `buf`.
+__device__ __forceinline__ void issue_qk(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf, int mt) {
   const uint64_t kst = md.k0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
+  const uint32_t d_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    const uint32_t d_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
-#pragma unroll
-    for (int ks = 0; ks < kD / 16; ++ks) {
-      const uint64_t a = md.q[mt][ks >> 2] + static_cast<uint64_t>((ks & 3) * 2);
-      const uint64_t b = kst + static_cast<uint64_t>((ks >> 2) * (kKVHalf >> 4) + (ks & 3) * 2);
-      umma_f16_ss(d_tmem, a, b, md.idesc_qk, ks > 0 ? 1u : 0u);
-    }
+  for (int ks = 0; ks < kD / 16; ++ks) {
+    const uint64_t a = md.q[mt][ks >> 2] + static_cast<uint64_t>((ks & 3) * 2);
+    const uint64_t b = kst + static_cast<uint64_t>((ks >> 2) * (kKVHalf >> 4) + (ks & 3) * 2);
+    umma_f16_ss(d_tmem, a, b, md.idesc_qk, ks > 0 ? 1u : 0u);
   }
 }
 
 // O_mt += P_mt (TMEM, over S buffer `buf`) * V (smem stage).
-__device__ __forceinline__ void issue_pv(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf,
+__device__ __forceinline__ void issue_pv(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf, int mt,
                                          uint32_t first) {
   const uint64_t vst = md.v0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
+  const uint32_t d_tmem = tmem + kColO + mt * kD;
+  const uint32_t p_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-    const uint32_t d_tmem = tmem + kColO + mt * kD;
-    const uint32_t p_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
-#pragma unroll
-    for (int ks = 0; ks < kBN / 16; ++ks) {
-      umma_f16_ts(d_tmem, p_tmem + ks * 8, vst + static_cast<uint64_t>(ks * (2048 >> 4)), md.idesc_pv,
-                  (ks > 0 || !first) ? 1u : 0u);
-    }
+  for (int ks = 0; ks < kBN / 16; ++ks) {
+    umma_f16_ts(d_tmem, p_tmem + ks * 8, vst + static_cast<uint64_t>(ks * (2048 >> 4)), md.idesc_pv,
+                (ks > 0 || !first) ? 1u : 0u);
   }
 }
 
@@ -307,14 +302,22 @@ __device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32
     if (!spin_wait(&bars->q_full, seg & 1u, abort)) break;
     bool ok = true;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
-      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort) ||
-          (i >= 2 && !spin_wait(&bars->p_free[i & 1u], ((i - 2) >> 1) & 1u, abort))) {
+      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      issue_qk(md, tmem, kr.stage, i & 1u);
-      umma_commit(&bars->s_full[i & 1u]);
+      // per M-tile: each softmax warpgroup starts as soon as its own half lands
+      for (int mt = 0; mt < 2 && ok; ++mt) {
+        const uint32_t bi = (i & 1u) * 2 + mt;
+        if (i >= 2 && !spin_wait(&bars->p_free[bi], ((i - 2) >> 1) & 1u, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_qk(md, tmem, kr.stage, i & 1u, mt);
+        umma_commit(&bars->s_full[bi]);
+      }
+      if (!ok) break;
       umma_commit(&bars->k_empty[kr.stage]);
       kr.next();
     }
@@ -337,14 +340,21 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32
     bool ok = true;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
       const uint32_t buf = i & 1u;
-      if (!spin_wait(&bars->p_full[buf], (i >> 1) & 1u, abort) ||
-          !spin_wait(&bars->v_full[vr.stage], vr.phase, abort)) {
+      if (!spin_wait(&bars->v_full[vr.stage], vr.phase, abort)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      issue_pv(md, tmem, vr.stage, buf, j == 0);
-      umma_commit(&bars->p_free[buf]);
+      for (int mt = 0; mt < 2 && ok; ++mt) {
+        const uint32_t bi = buf * 2 + mt;
+        if (!spin_wait(&bars->p_full[bi], (i >> 1) & 1u, abort)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(md, tmem, vr.stage, buf, mt, j == 0);
+        umma_commit(&bars->p_free[bi]);
+      }
+      if (!ok) break;
       umma_commit(&bars->v_empty[vr.stage]);
       vr.next();
     }
@@ -573,7 +583,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     float m_used = -INFINITY, l = 0.f;
     for (; g < e; ++g, ++i) {
       const uint32_t buf = static_cast<uint32_t>(i & 1);
-      if (!warp_wait(&bars->s_full[buf], static_cast<uint32_t>(i >> 1) & 1u, abort)) return;
+      if (!warp_wait(&bars->s_full[buf * 2 + wg], static_cast<uint32_t>(i >> 1) & 1u, abort)) return;
       tc_fence_after();
       float x[kBN];
       {
@@ -647,7 +657,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
-        if (!warp_wait(&bars->p_free[pv & 1], static_cast<uint32_t>(pv >> 1) & 1u, abort)) return;
+        if (!warp_wait(&bars->p_free[(pv & 1) * 2 + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort)) return;
         tc_fence_after();
         const uint32_t o_addr = lane_base + kColO + wg * kD;
 #pragma unroll
@@ -666,12 +676,12 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[buf]);
+      if (lane == 0) mbar_arrive(&bars->p_full[buf * 2 + wg]);
     }
 
     // ---- epilogue: O / l for this row, once the last P.V has landed
     const int64_t lastv = i - 1;
-    if (!warp_wait(&bars->p_free[lastv & 1], static_cast<uint32_t>(lastv >> 1) & 1u, abort)) return;
+    if (!warp_wait(&bars->p_free[(lastv & 1) * 2 + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort)) return;
     tc_fence_after();
     const bool whole = pi.start >= g0 && pi.end <= g1;
     const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
@@ -748,9 +758,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       mbar_init(&bars->v_empty[s], 1);
     }
     mbar_init(&bars->q_full, 8);
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < 4; ++b) {
       mbar_init(&bars->s_full[b], 1);
-      mbar_init(&bars->p_full[b], 8);
+      mbar_init(&bars->p_full[b], 4);  // the four warps of one softmax warpgroup
       mbar_init(&bars->p_free[b], 1);
     }
     mbar_init(&bars->drain[0], 1);
