@@ -34,6 +34,7 @@
 #include <cuda.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "attn.cuh"
 #include "sm100.cuh"
@@ -488,7 +489,7 @@ __device__ void combine_row(const TcArgs& t, int64_t first, int64_t last, int64_
   if (a.lse) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
 }
 
-template <int ANCW>
+template <int ANCW, bool BF16>
 __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
                                  int64_t g1, int64_t T, int cta) {
   const AttnArgs& a = t.a;
@@ -502,7 +503,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
   uint8_t* q_tile = smem + kOffQ + wg * 2 * kQHalf;
   const int R = a.group * a.n;
   const float sl2 = a.scale_log2;
-  const bool ab_bf16 = t.ab_fmt != 0;
+  constexpr bool ab_bf16 = BF16;  // P's 16-bit type (that of Q, K and V)
   const int qrow = wg * kBM + r;                // row within the pair's 256
   int64_t i = 0;
   for (int64_t g = g0; g < g1;) {
@@ -581,9 +582,15 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     if (!len_ok && qrow == 0) raise_device_error(a.err, kErrBadSeqlen);
 
     float m_used = -INFINITY, l = 0.f;
-    for (; g < e; ++g, ++i) {
+    // One tile of this row: S -> P against the lazy running max.  Masked
+    // tiles reach the tree rows or the sequence end and hide the columns this
+    // row may not see; the others (all but the last one or two of a pair) run
+    // a loop without that code, which keeps the hot loop's register
+    // allocation and schedule tight.
+    auto tile = [&](auto mask_tag) -> bool {
+      constexpr bool kMask = decltype(mask_tag)::value;
       const uint32_t buf = static_cast<uint32_t>(i & 1);
-      if (!warp_wait(&bars->s_full[buf * 2 + wg], static_cast<uint32_t>(i >> 1) & 1u, abort)) return;
+      if (!warp_wait(&bars->s_full[buf * 2 + wg], static_cast<uint32_t>(i >> 1) & 1u, abort)) return false;
       tc_fence_after();
       float x[kBN];
       {
@@ -598,13 +605,8 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
           x[32 + c] = __uint_as_float(r1[c]);
         }
       }
-      const int c0 = static_cast<int>(g - pi.start) * kBN;
-      // row max of the raw scores (scale > 0, so it commutes with max)
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (len_ok && c0 + kBN <= P) {
-#pragma unroll
-        for (int c = 0; c < kBN; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], x[c], x[c + 1]);
-      } else {
+      if (kMask) {
+        const int c0 = static_cast<int>(g - pi.start) * kBN;
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
           const int col = c0 + c;
@@ -612,9 +614,11 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
           const bool vis = len_ok && col < pi.L && (tt < 0 || anc_bit<ANCW>(anc, tt));
           x[c] = vis ? x[c] : -INFINITY;
         }
-#pragma unroll
-        for (int c = 0; c < kBN; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], x[c], x[c + 1]);
       }
+      // row max of the raw scores (scale > 0, so it commutes with max)
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < kBN; c += 2) mx[(c >> 1) & 3] = fmax3(mx[(c >> 1) & 3], x[c], x[c + 1]);
       const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * sl2;
       // lazy running max: move it only when this tile exceeds it by > 8
       float alpha = 1.f;
@@ -657,7 +661,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
-        if (!warp_wait(&bars->p_free[(pv & 1) * 2 + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort)) return;
+        if (!warp_wait(&bars->p_free[(pv & 1) * 2 + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort)) return false;
         tc_fence_after();
         const uint32_t o_addr = lane_base + kColO + wg * kD;
 #pragma unroll
@@ -677,7 +681,14 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->p_full[buf * 2 + wg]);
-    }
+      return true;
+    };
+    // tiles whose 64 columns all lie in the prefix before the tree rows
+    const int64_t plain_end = len_ok ? pi.start + P / kBN : pi.start;
+    for (; g < min(e, plain_end); ++g, ++i)
+      if (!tile(std::integral_constant<bool, false>())) return;
+    for (; g < e; ++g, ++i)
+      if (!tile(std::integral_constant<bool, true>())) return;
 
     // ---- epilogue: O / l for this row, once the last P.V has landed
     const int64_t lastv = i - 1;
@@ -740,7 +751,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
   }
 }
 
-template <int ANCW>
+template <int ANCW, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                const __grid_constant__ TcArgs t) {
@@ -802,7 +813,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     } else if (warp == 2) {
       if (lane == 0) pv_issuer(t, smem, bars, tmem, g0, g1);
     } else if (warp >= 4) {
-      softmax_epilogue<ANCW>(t, smem, bars, tmem, g0, g1, T, blockIdx.x);
+      softmax_epilogue<ANCW, BF16>(t, smem, bars, tmem, g0, g1, T, blockIdx.x);
     }
   }
   __syncwarp();  // role warps ran their loop on lane 0: reconverge before the CTA barrier
@@ -989,7 +1000,8 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
     rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
     if (rc) return rc;
   }
-  auto kern = a.n <= 64 ? attn_tc_kernel<2> : attn_tc_kernel<8>;
+  auto kern = a.n <= 64 ? (dtype == GORGON_BF16 ? attn_tc_kernel<2, true> : attn_tc_kernel<2, false>)
+                        : (dtype == GORGON_BF16 ? attn_tc_kernel<8, true> : attn_tc_kernel<8, false>);
   rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
                   "tcgen05 smem attribute");
   if (rc) return rc;
