@@ -44,8 +44,8 @@ from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
 NCU_TRAFFIC_BYTES = {
-    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.55 MB read + 3.50 MB written
-    ("verify-b16-p8192-n64", "tcgen05"): 553047552,
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.585 MB read + 3.880 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 553465600,
 }
 
 WORKLOADS = {
