@@ -38,7 +38,7 @@ sys.path.insert(0, str(ROOT))
 
 import projectgorgon_b200 as G  # noqa: E402
 from projectgorgon_b200 import sharding  # noqa: E402
-from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
+from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tree  # noqa: E402
 
 # Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
@@ -46,6 +46,13 @@ from projectgorgon_b200.trees import cartesian_tree, random_tree  # noqa: E402
 NCU_TRAFFIC_BYTES = {
     # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.585 MB read + 3.880 MB written
     ("verify-b16-p8192-n64", "tcgen05"): 553465600,
+    # profiles/verify_kernel_verifier-b32-n64-v128256.md: 533.673 MB read + 3.580 MB written
+    ("verifier-b32-n64-v128256", "verify_kernel"): 537253888,
+    # profiles/kv_trim_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.400 MB read, 0 written)
+    # scaled by 8 to 32 layers
+    ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11196416,
+    # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 2181.164 MB read + 7.039 MB written
+    ("wide-b8-p32k-n256", "tcgen05"): 2188202976,
 }
 
 WORKLOADS = {
@@ -57,6 +64,21 @@ WORKLOADS = {
                                  tree="cartesian", max_depth=31),
     "ragged-b16-p1k-8k-n64": dict(B=16, Hq=32, Hkv=8, D=128, P=(1024, 8192), N=64, dtype="bf16",
                                   tree="random", max_depth=5),
+    # 256-node best-first trees (top-4 over 4 levels) over a 32k prefix: the
+    # tensor-bound shape (arithmetic intensity ~1000 flop/byte)
+    "wide-b8-p32k-n256": dict(B=8, Hq=32, Hkv=8, D=128, P=32768, N=256, dtype="bf16",
+                              tree="best_first", max_depth=8, bound="tensor"),
+    # the fused verifier over one decode step's logits (65 rows: the root's
+    # row plus one per node) of a 128256-token vocabulary
+    "verifier-b32-n64-v128256": dict(kind="verify", B=32, N=64, V=128256, dtype="bf16", max_depth=5),
+    # trim-on-reject of the accepted path (<= 6 rows) in all 32 layers of a
+    # [32, 8, 4160, 128] bf16 K and V cache
+    "kvtrim-b32-l32-p4096": dict(kind="trim", B=32, layers=32, Hkv=8, D=128, P=4096, N=64, dtype="bf16",
+                                 max_depth=5),
+    # the same trim over 4 layers (2.2 GB of cache): small enough for a
+    # multi-pass profiler capture; its traffic scales with the layer count
+    "kvtrim-b32-l4-p4096": dict(kind="trim", B=32, layers=4, Hkv=8, D=128, P=4096, N=64, dtype="bf16",
+                                max_depth=5),
 }
 DEFAULT_WORKLOAD = "verify-b16-p8192-n64"
 TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
@@ -64,6 +86,15 @@ TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
 
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
+
+
+def make_tree(cfg: dict, rng: random.Random):
+    """The parents[] of one sequence's candidate tree."""
+    if cfg["tree"] == "random":
+        return random_tree(cfg["N"], rng, cfg["max_depth"])
+    if cfg["tree"] == "best_first":
+        return best_first_tree(rng, 4, 4, cfg["N"])[0]
+    return cartesian_tree(4, 2, True)
 
 
 # --------------------------------------------------------------------------
@@ -84,10 +115,7 @@ class Workload:
         self.ragged = isinstance(cfg["P"], tuple)
         rngs = [random.Random(1_000_003 + first_seq + j) for j in range(B)]
         self.prefixes = [r.randint(*cfg["P"]) if self.ragged else cfg["P"] for r in rngs]
-        if cfg["tree"] == "random":
-            self.parents = [random_tree(N, r, cfg["max_depth"]) for r in rngs]
-        else:
-            self.parents = [cartesian_tree(4, 2, True)] * B
+        self.parents = [make_tree(cfg, r) for r in rngs]
         self.max_depth = cfg["max_depth"]
         dt = TORCH_DT[cfg["dtype"]]
         self.dtype = dt
@@ -136,6 +164,274 @@ class Workload:
 
     def plan(self):
         return G.tree_attention_plan(self.q, self.k, self.v, **self.kwargs())
+
+    metric = "tree-verify HBM GB/s (algorithmic bytes / step time)"
+    data = "synthetic (seeded N(0,1)/sqrt(128) q/k/v, random trees)"
+
+    @property
+    def bound(self):
+        return self.cfg.get("bound", "hbm")
+
+    def config(self, world: int, plan: dict) -> dict:
+        cfg = self.cfg
+        return {
+            "workload": self.name, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"], "heads_kv": cfg["Hkv"],
+            "head_dim": cfg["D"], "prefix": cfg["P"] if not self.ragged else list(cfg["P"]),
+            "tree_nodes": cfg["N"], "tree": cfg["tree"], "max_depth": self.max_depth,
+            "mask": "parents (mask-free)",
+            "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+            "l2": f"inputs larger than L2 ({self.bytes / 1e6:.0f} MB per step per GPU)",
+            "backend": plan["backend"], "splits": plan["splits"],
+        }
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        return {"us_per_layer": round(ms_step * 1e3, 2),
+                "tokens_verified_per_s": round(world * self.tokens / (ms_step * 1e-3), 1)}
+
+    def e2e(self, steps: int, warmup: int, world: int):
+        ms, h2d, d2h = time_e2e(self, steps, warmup, world)
+        return ms, h2d, d2h, ("prefix K/V cache resident in HBM; per step the tree's Q, K/V rows and "
+                              "parents are copied in and the output copied out")
+
+    def cpu_baseline(self, budget_s: float):
+        return cpu_baseline(self, budget_s=budget_s)
+
+
+def _fill_normal(t: torch.Tensor, gen: torch.Generator, std: float) -> None:
+    """Fills a bf16/fp32 tensor with N(0, std) in 64 MB fp32 pieces."""
+    flat = t.view(-1)
+    step = 1 << 24
+    for s0 in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - s0)
+        flat[s0:s0 + n] = (torch.randn(n, device=t.device, generator=gen) * std).to(t.dtype)
+
+
+class VerifyWorkload:
+    """One decode step's tree verification (the fused verifier kernel):
+    logits [B, N + 1, V] bf16 ~ N(0, 2) (row 0 for the root, row 1 + t for
+    node t), random 64-node trees, drafts uniform over the vocabulary except
+    that about a quarter of the nodes, taken along random root-to-leaf paths
+    from the root, carry the argmax of their row, so accepted paths of every
+    length occur."""
+
+    metric = "tree verifier HBM GB/s (logits bytes / step time)"
+    data = "synthetic (seeded N(0,2) bf16 logits, random trees, drafts 1/4 on argmax paths)"
+    bound = "hbm"
+
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
+        cfg = WORKLOADS[name]
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, N, V = cfg["B"], cfg["N"], cfg["V"]
+        R = N + 1
+        rngs = [random.Random(2_000_003 + first_seq + j) for j in range(B)]
+        self.parents = [random_tree(N, r, cfg["max_depth"]) for r in rngs]
+        self.logits = torch.empty(B, R, V, device=dev, dtype=torch.bfloat16)
+        draft = torch.empty(B, N, dtype=torch.int64)
+        for j in range(B):
+            gen = torch.Generator(device=dev).manual_seed(3_000_003 + first_seq + j)
+            _fill_normal(self.logits[j], gen, 2.0)
+            pred = self.logits[j].float().argmax(-1).cpu()
+            g_cpu = torch.Generator().manual_seed(3_000_003 + first_seq + j)
+            draft[j] = torch.randint(0, V, (N,), generator=g_cpu)
+            par = self.parents[j]
+            children = [[] for _ in range(N)]
+            for t, p in enumerate(par):
+                if p >= 0:
+                    children[p].append(t)
+            marked, r = set(), rngs[j]
+            for _ in range(64 * N):
+                if len(marked) >= N // 4:
+                    break
+                t = 0
+                while True:
+                    marked.add(t)
+                    if not children[t] or len(marked) >= N // 4:
+                        break
+                    t = r.choice(children[t])
+            for t in marked:
+                draft[j, t] = pred[0 if par[t] < 0 else 1 + par[t]]
+        self.draft = draft.to(device=dev, dtype=torch.int32)
+        self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
+        self.bytes = (B * R * V * 2 + 2 * B * N * 4                     # logits, draft, parents
+                      + B * (R * 4 + N * 4 + 4 * 4))                    # pred, path, 4 per-sequence outputs
+        self.flops = 0
+        self.tokens = B * N
+
+    def step(self):
+        return G.verify_tree(self.logits, self.draft, self.par_t)
+
+    def plan(self):
+        return {"backend": "verify_kernel", "splits": None, "launches": 1}
+
+    def config(self, world: int, plan: dict) -> dict:
+        cfg = self.cfg
+        return {"workload": self.name, "batch_per_gpu": cfg["B"], "tree_nodes": cfg["N"],
+                "logits_rows": cfg["N"] + 1, "vocab": cfg["V"], "logits_dtype": "bf16",
+                "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                "l2": f"inputs larger than L2 ({self.bytes / 1e6:.0f} MB per step per GPU)",
+                "backend": plan["backend"]}
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        return {"us_per_step": round(ms_step * 1e3, 2),
+                "trees_verified_per_s": round(world * self.cfg["B"] / (ms_step * 1e-3), 1)}
+
+    def e2e(self, steps: int, warmup: int, world: int):
+        """Each step: drafts and parents in from pinned host memory, the
+        verifier, accepted lengths, paths and bonus tokens back out (the
+        logits stay on the device, where the model wrote them)."""
+        dev = self.dev
+        dr_h, par_h = self.draft.cpu().pin_memory(), self.par_t.cpu().pin_memory()
+        dr_d, par_d = torch.empty_like(self.draft), torch.empty_like(self.par_t)
+        B, N = self.cfg["B"], self.cfg["N"]
+        len_h = torch.empty(B, dtype=torch.int32).pin_memory()
+        path_h = torch.empty(B, N, dtype=torch.int32).pin_memory()
+        bonus_h = torch.empty(B, dtype=torch.int32).pin_memory()
+        h2d = (dr_h.numel() + par_h.numel()) * 4
+        d2h = (len_h.numel() + path_h.numel() + bonus_h.numel()) * 4
+
+        def one():
+            dr_d.copy_(dr_h, non_blocking=True)
+            par_d.copy_(par_h, non_blocking=True)
+            r = G.verify_tree(self.logits, dr_d, par_d)
+            len_h.copy_(r.accepted_len, non_blocking=True)
+            path_h.copy_(r.path, non_blocking=True)
+            bonus_h.copy_(r.bonus, non_blocking=True)
+
+        ms = _time_loop(one, dev, steps, warmup, world)
+        return ms, h2d, d2h, "logits resident in HBM (written there by the model); drafts and parents in, results out"
+
+    def cpu_baseline(self, budget_s: float):
+        from oracle import gorgon_oracle as O
+        B = self.cfg["B"]
+        times = []
+        t_start = time.perf_counter()
+        for j in range(B):
+            lg = self.logits[j].float().cpu().numpy()
+            dr = self.draft[j].cpu().tolist()
+            t0 = time.perf_counter()
+            O.verify_tree(lg, dr, self.parents[j])
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+        step_s = float(np.mean(times)) * B
+        return {"value": round(self.bytes / step_s / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "us_per_step": round(step_s * 1e6, 1),
+                "sample": (f"{len(times)} of {B} sequences through the oracle's verify_tree (numpy argmax "
+                           f"over all rows, then the path walk), extrapolated to the batch")}
+
+
+class TrimWorkload:
+    """Trim-on-reject after verification: for every layer, sequence and kv
+    head, the accepted path's K/V rows (root included, <= 6) move to the slots
+    right after the prefix, in place, in one launch over all layers."""
+
+    metric = "KV trim HBM GB/s (rows moved, read + write, / step time)"
+    data = "synthetic (seeded N(0,1) bf16 caches, random trees, random accepted paths)"
+    bound = "hbm"
+
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
+        from projectgorgon_b200.inference.kv_cache import GorgonKVCache
+        cfg = WORKLOADS[name]
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, Ly, H, D, P, N = cfg["B"], cfg["layers"], cfg["Hkv"], cfg["D"], cfg["P"], cfg["N"]
+        S = P + N
+        gen = torch.Generator(device=dev).manual_seed(4_000_003 + first_seq)
+        layers = []
+        for _ in range(Ly):
+            k = torch.empty(B, H, S, D, device=dev, dtype=torch.bfloat16)
+            v = torch.empty_like(k)
+            _fill_normal(k, gen, 1.0)
+            _fill_normal(v, gen, 1.0)
+            layers.append((k, v))
+        self.cache = GorgonKVCache()
+        self.cache.update(tuple(layers))
+        rngs = [random.Random(5_000_003 + first_seq + j) for j in range(B)]
+        idx = torch.zeros(B, cfg["max_depth"] + 1, dtype=torch.int32)
+        lens = torch.zeros(B, dtype=torch.int32)
+        for j, r in enumerate(rngs):
+            par = random_tree(N, r, cfg["max_depth"])
+            children = [[] for _ in range(N)]
+            for t, p in enumerate(par):
+                if p >= 0:
+                    children[p].append(t)
+            path, t = [0], 0
+            while children[t] and r.random() < 0.8:
+                t = r.choice(children[t])
+                path.append(t)
+            lens[j] = len(path)
+            idx[j, :len(path)] = torch.tensor([P + t for t in path], dtype=torch.int32)
+        self.idx, self.lens = idx.to(dev), lens.to(dev)
+        self.moved_rows = int(lens.sum())
+        self.bytes = 2 * 2 * self.moved_rows * H * D * 2 * Ly   # read + write of K and V rows
+        self.flops = 0
+        self.tokens = self.moved_rows
+
+    def step(self):
+        self.cache.trim(self.idx, self.lens, dst_start=self.cfg["P"])
+
+    def plan(self):
+        return {"backend": "kv_trim_kernel", "splits": None, "launches": 1}
+
+    def config(self, world: int, plan: dict) -> dict:
+        cfg = self.cfg
+        return {"workload": self.name, "batch_per_gpu": cfg["B"], "layers": cfg["layers"],
+                "heads_kv": cfg["Hkv"], "head_dim": cfg["D"], "prefix": cfg["P"],
+                "cache_seq": cfg["P"] + cfg["N"], "rows_moved_per_layer": self.moved_rows,
+                "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                "l2": f"each step moves scattered rows of a {2 * cfg['layers'] * cfg['B'] * cfg['Hkv'] * (cfg['P'] + cfg['N']) * cfg['D'] * 2 / 1e9:.1f} GB cache",
+                "backend": plan["backend"]}
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        return {"us_per_step": round(ms_step * 1e3, 2)}
+
+    def e2e(self, steps: int, warmup: int, world: int):
+        """Each step: the accepted source rows and lengths in from pinned host
+        memory, the trim, and the lengths back out."""
+        dev = self.dev
+        idx_h, lens_h = self.idx.cpu().pin_memory(), self.lens.cpu().pin_memory()
+        idx_d, lens_d = torch.empty_like(self.idx), torch.empty_like(self.lens)
+        out_h = torch.empty_like(lens_h).pin_memory()
+        h2d = (idx_h.numel() + lens_h.numel()) * 4
+        d2h = out_h.numel() * 4
+
+        def one():
+            idx_d.copy_(idx_h, non_blocking=True)
+            lens_d.copy_(lens_h, non_blocking=True)
+            self.cache.trim(idx_d, lens_d, dst_start=self.cfg["P"])
+            out_h.copy_(lens_d, non_blocking=True)
+
+        ms = _time_loop(one, dev, steps, warmup, world)
+        return ms, h2d, d2h, "cache resident in HBM; accepted rows and lengths in, lengths out"
+
+    def cpu_baseline(self, budget_s: float):
+        """The reference algorithm (clone of each layer's cache, then the row
+        gather: ``apply_cache_slice``) through the oracle on one layer of a few
+        sequences, extrapolated to all layers and sequences."""
+        from oracle import gorgon_oracle as O
+        cfg = self.cfg
+        nb = 4
+        k = self.cache.past_key_values[0][0][:nb].float().cpu().numpy()
+        v = self.cache.past_key_values[0][1][:nb].float().cpu().numpy()
+        idx = self.idx[:nb].cpu().numpy()
+        lens = self.lens[:nb].cpu().numpy()
+        ds = np.full(nb, cfg["P"], dtype=np.int64)
+        times = []
+        t_start = time.perf_counter()
+        while time.perf_counter() - t_start < min(budget_s, 5.0) or not times:
+            t0 = time.perf_counter()
+            O.kv_trim([(k, v)], idx, lens, ds)
+            times.append(time.perf_counter() - t0)
+        step_s = float(np.mean(times)) * (cfg["B"] / nb) * cfg["layers"]
+        return {"value": round(self.bytes / step_s / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "us_per_step": round(step_s * 1e6, 1),
+                "sample": (f"one layer of {nb} sequences through the oracle's kv_trim (the reference's "
+                           f"clone + gather), {len(times)} runs, extrapolated to {cfg['layers']} layers and "
+                           f"{cfg['B']} sequences")}
+
+
+def make_workload(name: str, dev: torch.device, first_seq: int = 0):
+    kind = WORKLOADS[name].get("kind", "attn")
+    return {"attn": Workload, "verify": VerifyWorkload, "trim": TrimWorkload}[kind](name, dev, first_seq)
 
 
 # --------------------------------------------------------------------------
@@ -223,7 +519,7 @@ def cpu_slices(cfg: dict, count: int, seed: int = 0):
     s = 1.0 / math.sqrt(D)
     for _ in range(count):
         P = prng.randint(*cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"]
-        par = random_tree(N, prng, cfg["max_depth"]) if cfg["tree"] == "random" else cartesian_tree(4, 2, True)
+        par = make_tree(cfg, prng)
         q = (rng.standard_normal((N, D), dtype=np.float32) * s)
         k = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
         v = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
@@ -362,16 +658,35 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     return e0.elapsed_time(e1), h2d, d2h
 
 
+def _time_loop(one, dev, steps: int, warmup: int, world: int) -> float:
+    """Device time (ms) of `steps` calls of `one` after `warmup` untimed ones."""
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(steps):
+        one()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1)
+
+
 def max_over_ranks(x: float, world: int, dev) -> float:
     return sharding.max_over_ranks(x, dev) if world > 1 else x
 
 
 def peaks():
+    """(HBM GB/s, burst bf16 TFLOP/s, source): measured on this pool's B200s
+    when MEASURED_PEAKS.json is present, else the earlier pool measurement."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
 
 
 def run_ours(args):
@@ -383,14 +698,14 @@ def run_ours(args):
     sharding.init(sharding.dist_env(), "nccl", dev, timeout_s=120)
     G.load_library()
     # weak scaling by sequence: rank r verifies global sequences [r*B, (r+1)*B)
-    wl = Workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
+    wl = make_workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
     plan = wl.plan()
     total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
     total_ms = max_over_ranks(total_ms, world, dev)
     launch_ms = max_over_ranks(launch_ms, world, dev)
-    e2e_ms, h2d, d2h = time_e2e(wl, args.e2e_steps or args.steps, args.warmup, world)
-    e2e_ms = max_over_ranks(e2e_ms, world, dev)
     e2e_steps = args.e2e_steps or args.steps
+    e2e_ms, h2d, d2h, e2e_note = wl.e2e(e2e_steps, args.warmup, world)
+    e2e_ms = max_over_ranks(e2e_ms, world, dev)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -399,11 +714,26 @@ def run_ours(args):
     ms_step = total_ms / args.steps
     value = world * wl.bytes * args.steps / (total_ms * 1e-3) / 1e9
     e2e_val = world * wl.bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
-    peak, peak_kind = peaks()
-    achieved = wl.bytes / (launch_ms * 1e-3) / 1e9
-    cfg = wl.cfg
+    hbm_peak, tc_peak, peak_kind = peaks()
+    if wl.bound == "tensor":
+        achieved = wl.flops / (launch_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tc_peak, "unit": "TFLOP/s",
+                "frac": round(achieved / tc_peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)" if peak_kind == "measured"
+                else "fallback 1590 TFLOP/s", "algorithmic_flops": wl.flops,
+                "hbm_gbs": round(wl.bytes / (launch_ms * 1e-3) / 1e9, 2)}
+    else:
+        achieved = wl.bytes / (launch_ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6650 GB/s"}
+        if wl.flops:
+            roof["tflops"] = round(wl.flops / (launch_ms * 1e-3) / 1e12, 2)
+    roof.update({"traffic": NCU_TRAFFIC_BYTES.get((wl.name, plan["backend"])),
+                 "launch_us": round(launch_ms * 1e3, 3), "algorithmic_bytes": wl.bytes})
     out = {
-        "metric": "tree-verify HBM GB/s (algorithmic bytes / step time)",
+        "metric": wl.metric,
         "value": round(value, 2),
         "unit": "GB/s",
         "n_gpus": world,
@@ -413,39 +743,21 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": cfg["dtype"],
-        "data": "synthetic (seeded N(0,1)/sqrt(128) q/k/v, random trees)",
-        "config": {
-            "workload": wl.name, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"], "heads_kv": cfg["Hkv"],
-            "head_dim": cfg["D"], "prefix": cfg["P"] if not wl.ragged else list(cfg["P"]),
-            "tree_nodes": cfg["N"], "max_depth": wl.max_depth, "mask": "parents (mask-free)",
-            "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-            "l2": f"inputs larger than L2 ({wl.bytes / 1e6:.0f} MB per step per GPU)",
-            "backend": plan["backend"], "splits": plan["splits"],
-        },
-        "us_per_layer": round(ms_step * 1e3, 2),
+        "dtype": wl.cfg["dtype"],
+        "data": wl.data,
+        "config": wl.config(world, plan),
         "pct_of_8tbs": round(100.0 * value / world / 8000.0, 2),
-        "tokens_verified_per_s": round(world * wl.tokens / (ms_step * 1e-3), 1),
-        "roofline": {
-            "bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-            if peak_kind == "measured" else "fallback 6650 GB/s",
-            "traffic": NCU_TRAFFIC_BYTES.get((wl.name, plan["backend"])),
-            "launch_us": round(launch_ms * 1e3, 3),
-            "algorithmic_bytes": wl.bytes,
-            "tflops": round(wl.flops / (launch_ms * 1e-3) / 1e12, 2),
-        },
+        "roofline": roof,
         "e2e": {
             "value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 5),
-            "note": "prefix K/V cache resident in HBM; per step the tree's Q, K/V rows and "
-                    "parents are copied in and the output copied out",
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 5), "note": e2e_note,
         },
         "gpu_launches": plan["launches"] * args.steps,
         "clocks": clocks,
     }
+    out.update(wl.extra(world, ms_step))
     if world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(wl, budget_s=args.cpu_budget)
+        out["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
     print(json.dumps(out), flush=True)
 
 
@@ -457,6 +769,9 @@ def run_reference(args):
         return
     from oracle import gorgon_oracle as O
     cfg = WORKLOADS[args.workload]
+    if cfg.get("kind", "attn") != "attn":
+        run_reference_other(args, cfg, world)
+        return
     cores = blas_threads()
     inputs = list(cpu_slices(cfg, 8, seed=0))
     total_slices = cfg["B"] * cfg["Hq"]
@@ -488,6 +803,66 @@ def run_reference(args):
                          "sample": "each step one (batch, q-head) slice of the workload through the "
                                    "oracle's tree_attention (fp32 numpy/BLAS), extrapolated by kv "
                                    "rows to the full layer"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def run_reference_other(args, cfg: dict, world: int):
+    """Reference arm of the verifier and trim workloads: the oracle's
+    verify_tree (one sequence per step) or kv_trim (one layer of four
+    sequences per step, the reference's clone + gather) on host-generated
+    inputs of the workload's shapes, extrapolated to the whole step."""
+    from oracle import gorgon_oracle as O
+    rng = np.random.default_rng(0)
+    prng = random.Random(0)
+    B, N = cfg["B"], cfg["N"]
+    if cfg["kind"] == "verify":
+        V, R = cfg["V"], cfg["N"] + 1
+        wl_bytes = B * R * V * 2 + 2 * B * N * 4 + B * (R * 4 + N * 4 + 16)
+        metric, what = VerifyWorkload.metric, "one sequence through the oracle's verify_tree, x batch"
+
+        def sample():
+            lg = rng.standard_normal((R, V), dtype=np.float32) * 2.0
+            return lg, rng.integers(0, V, N).tolist(), random_tree(N, prng, cfg["max_depth"])
+
+        def run(s):
+            O.verify_tree(*s)
+        scale = B
+    else:
+        nb, H, D, P = 4, cfg["Hkv"], cfg["D"], cfg["P"]
+        S = P + N
+        rows = 6 * B
+        wl_bytes = 2 * 2 * rows * H * D * 2 * cfg["layers"]
+        metric, what = TrimWorkload.metric, (f"one layer of {nb} sequences through the oracle's kv_trim "
+                                             f"(clone + gather), x {B // nb} x {cfg['layers']} layers")
+
+        def sample():
+            k = rng.standard_normal((nb, H, S, D), dtype=np.float32)
+            v = rng.standard_normal((nb, H, S, D), dtype=np.float32)
+            idx = np.tile(np.arange(P, P + 6, dtype=np.int64), (nb, 1))
+            return k, v, idx, np.full(nb, 6), np.full(nb, P)
+
+        def run(s):
+            k, v, idx, lens, ds = s
+            O.kv_trim([(k, v)], idx, lens, ds)
+        scale = (B / nb) * cfg["layers"]
+    s = sample()
+    for _ in range(args.warmup):
+        run(s)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run(s)
+        times.append((time.perf_counter() - t0) * scale)
+    step_s = float(np.mean(times))
+    value = wl_bytes / step_s / 1e9
+    out = {
+        "impl": "reference", "metric": metric, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": "synthetic", "config": {"workload": args.workload, "batch_per_gpu": B},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": 1, "kind": "port", "sample": what},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
