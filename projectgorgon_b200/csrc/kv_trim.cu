@@ -83,6 +83,60 @@ __global__ void __launch_bounds__(kThreads) kv_trim_kernel(const TrimArgs a) {
   }
 }
 
+// Fast path for the common case (16-byte aligned rows, at most kRegChunks * 32
+// 16-byte chunks per slice, e.g. 16 rows of 256 bytes): one warp per (layer,
+// K/V, batch row, head) slice, kWarps heads per CTA, so the whole trim of a
+// decode step is one wave of CTAs.  Lengths, destination starts and indices
+// are fetched together (indices up to max_len, unconditionally in range of the
+// index row), the slice's source rows go to registers, a warp barrier orders
+// every lane's loads before any lane's stores (in-place moves whose slots
+// overlap later sources stay correct), then the rows are written.
+constexpr int kWarps = 8;
+constexpr int kRegChunks = 8;
+
+__global__ void __launch_bounds__(kWarps * 32) kv_trim_warp_kernel(const TrimArgs a, int heads) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.x * kWarps + warp;
+  const int b = blockIdx.y;
+  const int layer = blockIdx.z >> 1;
+  const int kv = blockIdx.z & 1;
+  if (h >= heads) return;
+  const int32_t* ib = a.idx + static_cast<int64_t>(b) * a.idx_sb;
+  const int len = a.lens[b];
+  const int d0 = a.dst_start ? a.dst_start[b] : 0;
+  const int my_src = lane < a.max_len ? ib[lane] : 0;  // max_len <= 32 on this path
+  int bad = (len < 0 || len > a.max_len || d0 < 0 || static_cast<int64_t>(d0) + max(len, 0) > a.seq);
+  if (!bad && lane < len && (my_src < 0 || my_src >= a.seq)) bad = 1;
+  if (__any_sync(0xffffffffu, bad)) {
+    if (lane == 0 && h == 0 && blockIdx.z == 0) raise_device_error(a.err, kErrBadTrimIndex);
+    return;
+  }
+  if (len == 0) return;
+  const int64_t slice = (static_cast<int64_t>(b) * a.sb + static_cast<int64_t>(h) * a.sh) * a.elem_bytes;
+  const char* src = static_cast<const char*>(a.src[kv][layer]) + slice;
+  char* dst = static_cast<char*>(a.dst[kv][layer]) + slice;
+  const int64_t rs = a.ss * a.elem_bytes;
+  const int vpr = static_cast<int>(a.row_bytes / 16);
+  const int total = len * vpr;
+  uint4 v[kRegChunks];
+#pragma unroll
+  for (int k = 0; k < kRegChunks; ++k) {
+    const int e = lane + 32 * k;
+    const int r = e / vpr;
+    const int s = __shfl_sync(0xffffffffu, my_src, min(r, 31));  // every lane, one program point
+    if (e < total) v[k] = __ldcs(reinterpret_cast<const uint4*>(src + s * rs + (e - r * vpr) * 16));
+  }
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < kRegChunks; ++k) {
+    const int e = lane + 32 * k;
+    if (e < total) {
+      const int r = e / vpr, c = e - r * vpr;
+      *reinterpret_cast<uint4*>(dst + (d0 + r) * rs + c * 16) = v[k];
+    }
+  }
+}
+
 }  // namespace
 }  // namespace gorgon
 
@@ -120,13 +174,29 @@ extern "C" int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream) {
     }
   }
   a.vec_ok = vec;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vec && p->max_len <= 32 && p->max_len * (row_bytes / 16) <= 32 * kRegChunks) {
+    for (int64_t l0 = 0; l0 < p->layers; l0 += kLayersPerLaunch) {
+      const int nl = static_cast<int>(std::min<int64_t>(kLayersPerLaunch, p->layers - l0));
+      for (int i = 0; i < nl; ++i) {
+        a.src[0][i] = p->k_src[l0 + i];
+        a.src[1][i] = p->v_src[l0 + i];
+        a.dst[0][i] = p->k_dst ? p->k_dst[l0 + i] : p->k_src[l0 + i];
+        a.dst[1][i] = p->v_dst ? p->v_dst[l0 + i] : p->v_src[l0 + i];
+      }
+      dim3 grid(static_cast<unsigned>((p->heads + kWarps - 1) / kWarps), static_cast<unsigned>(p->batch), 2u * nl);
+      kv_trim_warp_kernel<<<grid, kWarps * 32, 0, st>>>(a, static_cast<int>(p->heads));
+      int rc = check_cuda(cudaGetLastError(), "kv_trim launch");
+      if (rc) return rc;
+    }
+    return GORGON_OK;
+  }
   auto kern = kv_trim_kernel;
   if (smem > 48 * 1024) {
     int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(smem)), "kv_trim smem attribute");
     if (rc) return rc;
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int64_t l0 = 0; l0 < p->layers; l0 += kLayersPerLaunch) {
     const int nl = static_cast<int>(std::min<int64_t>(kLayersPerLaunch, p->layers - l0));
     for (int i = 0; i < nl; ++i) {

@@ -25,7 +25,6 @@ def _launch_trim(k_src: List[torch.Tensor], v_src: List[torch.Tensor],
                  batch: int, heads: int, seq: int, head_dim: int, strides: Tuple[int, int, int],
                  elem_bytes: int, idx: torch.Tensor, lens: torch.Tensor,
                  dst_start: Optional[torch.Tensor]) -> None:
-    dev = k_src[0].device
     p = _abi.KvTrimParams()
     p.elem_bytes = elem_bytes
     p.layers, p.batch, p.heads, p.seq_capacity, p.head_dim = len(k_src), batch, heads, seq, head_dim
@@ -37,9 +36,18 @@ def _launch_trim(k_src: List[torch.Tensor], v_src: List[torch.Tensor],
         arrays += [_abi.pointer_array([t.data_ptr() for t in k_dst]),
                    _abi.pointer_array([t.data_ptr() for t in v_dst])]
         p.k_dst, p.v_dst = arrays[2], arrays[3]
+    _run_trim(p, k_src[0].device, idx, lens, dst_start)
+
+
+def _run_trim(p, dev: torch.device, idx: torch.Tensor, lens: torch.Tensor,
+              dst_start: Optional[torch.Tensor]) -> None:
+    """Fills the per-call fields of a prepared parameter block and launches."""
     p.src_idx, p.idx_stride_b, p.max_len = idx.data_ptr(), idx.stride(0), idx.shape[1]
     p.lens = lens.data_ptr()
     p.dst_start = dst_start.data_ptr() if dst_start is not None else 0
+    if torch.cuda.current_device() == dev.index:
+        _abi.check(_abi.lib().gorgon_kv_trim(p, stream_ptr(dev)), "gorgon_kv_trim")
+        return
     with torch.cuda.device(dev):
         _abi.check(_abi.lib().gorgon_kv_trim(p, stream_ptr(dev)), "gorgon_kv_trim")
 
@@ -99,6 +107,8 @@ class GorgonKVCache:
         self._cache: Optional[PastKV] = None
         self._checkpoint: Optional[PastKV] = None
         self._seq_len: int = 0
+        self._trim_plan = None   # validated layout + per-layer pointer arrays of the current cache
+        self._dst_fill = {}      # (batch, start) -> device int32 [batch] filled with start
 
     @property
     def past_key_values(self) -> Optional[PastKV]:
@@ -150,15 +160,10 @@ class GorgonKVCache:
         ``dst_start`` is ``[B]``, an int, or None for 0."""
         if self._cache is None:
             return
+        params = self._prepared_trim()
         k0 = self._cache[0][0]
-        require_cuda("cache tensors", k0)
         dev = k0.device
-        B, H, S, D = k0.shape
-        for k, v in self._cache:
-            if k.shape != k0.shape or v.shape != k0.shape or k.dtype != k0.dtype or v.dtype != k0.dtype:
-                raise RuntimeError("all layers must share one shape and dtype")
-            if k.stride() != k0.stride() or v.stride() != k0.stride() or k.stride(-1) != 1:
-                raise RuntimeError("all layers must share one stride layout with head_dim contiguous")
+        B = k0.shape[0]
         idx = src_idx.to(device=dev, dtype=torch.int32)
         if idx.dim() == 1:
             idx = idx.unsqueeze(0)
@@ -167,11 +172,40 @@ class GorgonKVCache:
         if idx.shape[0] != B or ln.numel() != B:
             raise RuntimeError("src_idx and lens need one row per batch element")
         if isinstance(dst_start, int):
-            ds = torch.full((B,), dst_start, dtype=torch.int32, device=dev)
+            ds = self._dst_fill.get((B, dst_start))
+            if ds is None or ds.device != dev:
+                ds = torch.full((B,), dst_start, dtype=torch.int32, device=dev)
+                self._dst_fill[(B, dst_start)] = ds
         elif dst_start is None:
             ds = None
         else:
             ds = dst_start.to(device=dev, dtype=torch.int32).reshape(-1).contiguous()
-        st = k0.stride()
-        _launch_trim([k for k, _ in self._cache], [v for _, v in self._cache], None, None,
-                     B, H, S, D, (st[0], st[1], st[2]), k0.element_size(), idx, ln, ds)
+        _run_trim(params, dev, idx, ln, ds)
+
+    def _prepared_trim(self):
+        """The trim's parameter block for the current layers: the layout is
+        checked and the per-layer pointer arrays built once per cache (the
+        cache tuple is replaced, never mutated, by update/rollback/trim_to)."""
+        c = self._cache
+        plan = self._trim_plan
+        if plan is not None and plan[0] is c and plan[1] == c[0][0].data_ptr():
+            return plan[2]
+        k0 = c[0][0]
+        require_cuda("cache tensors", k0)
+        B, H, S, D = k0.shape
+        for k, v in c:
+            if k.shape != k0.shape or v.shape != k0.shape or k.dtype != k0.dtype or v.dtype != k0.dtype:
+                raise RuntimeError("all layers must share one shape and dtype")
+            if k.stride() != k0.stride() or v.stride() != k0.stride() or k.stride(-1) != 1:
+                raise RuntimeError("all layers must share one stride layout with head_dim contiguous")
+            if k.device != k0.device or v.device != k0.device:
+                raise RuntimeError("all layers must be on one device")
+        p = _abi.KvTrimParams()
+        p.elem_bytes = k0.element_size()
+        p.layers, p.batch, p.heads, p.seq_capacity, p.head_dim = len(c), B, H, S, D
+        p.stride_b, p.stride_h, p.stride_s = k0.stride(0), k0.stride(1), k0.stride(2)
+        arrays = (_abi.pointer_array([k.data_ptr() for k, _ in c]),
+                  _abi.pointer_array([v.data_ptr() for _, v in c]))
+        p.k_src, p.v_src = arrays
+        self._trim_plan = (c, k0.data_ptr(), p, arrays)   # the arrays stay alive with the block
+        return p

@@ -57,6 +57,31 @@ def test_all_layer_in_place_trim(dtype, D):
         np.testing.assert_array_equal(v.float().cpu().numpy(), wv)
 
 
+@pytest.mark.parametrize("max_len", [16, 17])
+def test_in_place_trim_at_the_register_path_limit(max_len):
+    """16 accepted rows of 256 bytes fill the warp path's registers exactly;
+    17 take the shared-memory path.  11 heads leave a partly used CTA, and
+    every destination slot overlaps a later source row."""
+    Lyr, B, H, D, P = 2, 3, 11, 128, 20
+    S = P + 2 * max_len + 5
+    g = torch.Generator(device="cuda").manual_seed(max_len)
+    layers = [(torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16(),
+               torch.randn(B, H, S, D, device="cuda", generator=g).bfloat16()) for _ in range(Lyr)]
+    ref_in = [(k.float().cpu().numpy(), v.float().cpu().numpy()) for k, v in layers]
+    idx = np.zeros((B, max_len), dtype=np.int32)
+    lens = np.array([max_len, max_len - 3, 1], dtype=np.int32)
+    for b in range(B):
+        idx[b, :lens[b]] = [P + 2 * r + 1 for r in range(lens[b])]  # row P + r <- row P + 2r + 1
+    dst = np.full(B, P, dtype=np.int32)
+    cache = G.GorgonKVCache()
+    cache.update(tuple(layers))
+    cache.trim(torch.from_numpy(idx).cuda(), torch.from_numpy(lens).cuda(), P)
+    want = O.kv_trim(ref_in, idx, lens, dst)
+    for (k, v), (wk, wv) in zip(cache.past_key_values, want):
+        np.testing.assert_array_equal(k.float().cpu().numpy(), wk)
+        np.testing.assert_array_equal(v.float().cpu().numpy(), wv)
+
+
 def test_trim_from_verifier_outputs_without_host_sync():
     """verify_tree's device path feeds KVCache.trim directly (idx = P + path)."""
     B, n, V, P, H, D = 3, 8, 300, 20, 2, 16
