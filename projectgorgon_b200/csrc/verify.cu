@@ -59,9 +59,89 @@ __device__ __forceinline__ bool arg_better(float v1, int i1, float v2, int i2) {
   return i1 < i2;
 }
 
+// 16-bit logits: packed pair types and their NaN-propagating max.
+template <typename T> struct Pair16;
+template <> struct Pair16<__nv_bfloat16> {
+  using P = __nv_bfloat162;
+  static __device__ __forceinline__ P max_nan(P a, P b) { return __hmax2_nan(a, b); }
+  static __device__ __forceinline__ float lo(P p) { return __low2float(p); }
+  static __device__ __forceinline__ float hi(P p) { return __high2float(p); }
+};
+template <> struct Pair16<__half> {
+  using P = __half2;
+  static __device__ __forceinline__ P max_nan(P a, P b) { return __hmax2_nan(a, b); }
+  static __device__ __forceinline__ float lo(P p) { return __low2float(p); }
+  static __device__ __forceinline__ float hi(P p) { return __high2float(p); }
+};
+
+// Thread's argmax over its 16-byte chunks of a 16-bit row (chunks v, v +
+// kThreads, ...; the caller handles the vocabulary tail).  Per chunk the 8
+// values fold into one with packed NaN-propagating maxima; the thread keeps
+// the largest chunk maximum and the first chunk that reached it (NaN above
+// everything, ties to the earlier chunk), then reads that chunk again (an L2
+// hit) for the first element equal to its maximum.  Same result as ranking
+// every element with arg_better, at about one instruction per element pair.
+template <typename T>
+__device__ __forceinline__ void scan_chunks16(const uint4* __restrict__ rv, int64_t nvec, float& bv, int& bi) {
+  using PT = Pair16<T>;
+  using P = typename PT::P;
+  float rm = -INFINITY;
+  int64_t rc = -1;
+  constexpr int U = 4;
+  int64_t v = threadIdx.x;
+  auto fold = [&](const uint4& raw, int64_t idx) {
+    const P* p = reinterpret_cast<const P*>(&raw);
+    const P m = PT::max_nan(PT::max_nan(p[0], p[1]), PT::max_nan(p[2], p[3]));
+    const float a = PT::lo(m), b = PT::hi(m);
+    const float cm = (isnan(a) || isnan(b)) ? NAN : fmaxf(a, b);
+    const bool better = rc < 0 || (isnan(cm) ? !isnan(rm) : cm > rm);
+    if (better) {
+      rm = cm;
+      rc = idx;
+    }
+  };
+  for (; v + (U - 1) * kThreads < nvec; v += U * kThreads) {
+    uint4 raw[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) raw[u] = __ldcs(rv + v + u * kThreads);
+#pragma unroll
+    for (int u = 0; u < U; ++u) fold(raw[u], v + u * kThreads);
+  }
+  for (; v < nvec; v += kThreads) fold(__ldcs(rv + v), v);
+  if (rc < 0) return;
+  const uint4 raw = rv[rc];
+  const T* e = reinterpret_cast<const T*>(&raw);
+  int q = 0;
+  float x = rm;
+#pragma unroll
+  for (int k = 7; k >= 0; --k) {
+    const float xk = Cvt<T>::to_f(e[k]);
+    if (isnan(rm) ? isnan(xk) : xk == rm) {
+      q = k;
+      x = xk;
+    }
+  }
+  const int idx = static_cast<int>(rc * 8 + q);
+  if (arg_better(x, idx, bv, bi)) {
+    bv = x;
+    bi = idx;
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ void scan_row(const T* __restrict__ row, int64_t vocab, bool vec_ok,
                                          float& bv, int& bi) {
+  if constexpr (sizeof(T) == 2) {
+    if (vec_ok) {
+      const int64_t nvec = vocab / 8;
+      scan_chunks16<T>(reinterpret_cast<const uint4*>(row), nvec, bv, bi);
+      for (int64_t c = nvec * 8 + threadIdx.x; c < vocab; c += kThreads) {
+        const float x = Cvt<T>::to_f(row[c]);
+        if (arg_better(x, static_cast<int>(c), bv, bi)) { bv = x; bi = static_cast<int>(c); }
+      }
+      return;
+    }
+  }
   constexpr int EV = 16 / sizeof(T);
   int64_t start = 0;
   if (vec_ok) {

@@ -116,6 +116,39 @@ def test_argmax_ties_and_nan_follow_torch():
     assert int(r.accepted_len) == 2
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_argmax_edge_rows_in_every_logits_type(dtype):
+    """Rows that separate a chunked scan from an element-by-element one:
+    ties inside one 16-byte chunk, across two chunks of the same thread
+    (2048 values apart with 256 threads x 8 values) and across threads; all
+    -inf; NaN anywhere beats everything and the first NaN wins; -0 equals +0;
+    the maximum, or the only NaN, in the vocabulary tail (V % 8 == 3)."""
+    V = 4099
+    rows = torch.full((8, V), -1.0)
+    rows[0, 17] = 5.0
+    rows[0, 4000] = 5.0                       # tie across threads
+    rows[1, :] = -float("inf")
+    rows[2, 100] = float("nan")
+    rows[2, 200] = float("nan")
+    rows[2, 7] = 9.0
+    rows[3, 2050] = -0.0
+    rows[3, 9] = 0.0                          # -0 == +0: first index
+    rows[4, 4098] = 7.0                       # in the tail
+    rows[5, 8 * 40 + 5] = 3.0
+    rows[5, 8 * 40 + 2] = 3.0                 # tie inside one chunk
+    rows[6, 8 * 100 + 1] = 2.0
+    rows[6, 8 * (100 + 256)] = 2.0            # tie across two chunks of one thread
+    rows[7, 10] = 100.0
+    rows[7, 4097] = float("nan")              # the only NaN, in the tail
+    logits = rows.to(dtype).cuda()
+    n = 7
+    r = G.verify_tree(logits, torch.zeros(n, dtype=torch.int32, device="cuda"), [-1] + list(range(n - 1)),
+                      prompt_len=1)
+    want = torch.argmax(logits.float().cpu(), -1).tolist()
+    assert want == [17, 0, 100, 9, 4098, 322, 801, 4097]
+    assert r.pred.tolist() == want
+
+
 def test_unsorted_forest_and_bad_parent():
     par = [3, -1, 1, -1, 3, 0, 0]
     V, pl = 11, 2
