@@ -9,8 +9,8 @@
 // SMs, each CTA takes whole pairs.  Otherwise (stream-K) the pair-major list
 // of 64-row key/value tiles is split into equal contiguous ranges: a pair
 // that falls inside one CTA is finished there; a pair cut between CTAs leaves
-// normalised partials plus log-sum-exp in the workspace and the CTA that
-// finishes it last merges them (no spinning: an atomic arrival count).
+// normalised partials plus log-sum-exp in the workspace, and attn_tc_combine,
+// launched right after, merges them with one warp per row.
 //
 // Warp roles (384 threads):
 //   warp 0       TMA producer for K tiles (two 64-column SW128 boxes), 5-stage ring
@@ -79,7 +79,6 @@ struct TcArgs {
   int pair_align;     // CTA ranges hold whole pairs (no partials to merge)
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // bf16 output with 16-byte aligned rows
-  int* counters;      // [pairs][8] arrivals of partial pairs, per softmax warp
   float* part_o;      // [grid * 2][256][128]
   float* part_lse;    // [grid * 2][256]
   int* tile_start;    // varlen: [pairs + 1] tile prefix (written by attn_tc_prologue)
@@ -199,8 +198,11 @@ __device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem,
   int64_t issued = 0;
   int cur_pair = -1;
   PairInfo pi{};
-  // K/V are read once: keep them from pushing the partial results out of L2
-  const uint64_t policy = l2_policy_evict_first();
+  // With one query group per (sequence, kv head) K/V are read once: keep them
+  // from pushing the partial results out of L2.  With several, the groups'
+  // CTAs run side by side over the same K/V, and the later ones should find
+  // it in L2.
+  const uint64_t policy = t.qgroups > 1 ? l2_policy_evict_last() : l2_policy_evict_first();
   for (int64_t g = g0; g < g1; ++g) {
     const int p = pair_of(t, g);
     if (p != cur_pair) {
@@ -401,93 +403,6 @@ __device__ __forceinline__ void store_cols32(const TcArgs& t, int64_t ob, int co
   }
 }
 
-// Merges the partials of one row of a pair that was cut between CTAs
-// first..last: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M).  All
-// loads of a 32-column chunk are issued before any is used.
-__device__ void combine_row(const TcArgs& t, int64_t first, int64_t last, int64_t pstart, int64_t T, int qrow,
-                            bool row_ok, int64_t ob, int64_t orow) {
-  constexpr int kMaxParts = 4;
-  const int parts = static_cast<int>(last - first + 1);
-  auto slot_of = [&](int64_t c) -> int64_t {
-    return c * 2 + ((c == first && pstart > range_start(c, T, t.grid)) ? 1 : 0);
-  };
-  float M = -INFINITY;
-  float lse_k[kMaxParts];
-  int64_t sl_k[kMaxParts];
-#pragma unroll
-  for (int k = 0; k < kMaxParts; ++k) {
-    sl_k[k] = k < parts ? slot_of(first + k) : 0;
-    lse_k[k] = k < parts ? __ldcg(t.part_lse + sl_k[k] * kQRows + qrow) : -INFINITY;
-  }
-  for (int64_t c = first + kMaxParts; c <= last; ++c) M = fmaxf(M, __ldcg(t.part_lse + slot_of(c) * kQRows + qrow));
-#pragma unroll
-  for (int k = 0; k < kMaxParts; ++k) M = fmaxf(M, lse_k[k]);
-  if (!row_ok) return;
-  const AttnArgs& a = t.a;
-  if (M == -INFINITY) {
-    for (int c = 0; c < kD; ++c) store_as(a.out, a.out_dtype, ob + c, NAN);
-    if (a.lse) a.lse[orow] = -INFINITY;
-    return;
-  }
-  float w_k[kMaxParts];
-  float wsum = 0.f;
-#pragma unroll
-  for (int k = 0; k < kMaxParts; ++k) {
-    w_k[k] = k < parts ? ex2_approx(lse_k[k] - M) : 0.f;
-    wsum += w_k[k];
-  }
-  for (int64_t c = first + kMaxParts; c <= last; ++c) wsum += ex2_approx(__ldcg(t.part_lse + slot_of(c) * kQRows + qrow) - M);
-  const float winv = 1.f / wsum;
-#pragma unroll 1
-  for (int ch = 0; ch < kD; ch += 64) {
-    float acc[64];
-#pragma unroll
-    for (int c = 0; c < 64; ++c) acc[c] = 0.f;
-    {
-      // the first two parts (the common case) with every load in flight
-      float4 v0[16], v1[16];
-      const float4* s0 = reinterpret_cast<const float4*>(t.part_o + (sl_k[0] * kQRows + qrow) * kD + ch);
-      const float4* s1 = reinterpret_cast<const float4*>(t.part_o + (sl_k[1] * kQRows + qrow) * kD + ch);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        v0[q] = __ldcg(s0 + q);
-        v1[q] = parts > 1 ? __ldcg(s1 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        acc[4 * q] = fmaf(w_k[0], v0[q].x, fmaf(w_k[1], v1[q].x, acc[4 * q]));
-        acc[4 * q + 1] = fmaf(w_k[0], v0[q].y, fmaf(w_k[1], v1[q].y, acc[4 * q + 1]));
-        acc[4 * q + 2] = fmaf(w_k[0], v0[q].z, fmaf(w_k[1], v1[q].z, acc[4 * q + 2]));
-        acc[4 * q + 3] = fmaf(w_k[0], v0[q].w, fmaf(w_k[1], v1[q].w, acc[4 * q + 3]));
-      }
-    }
-    for (int64_t c = first + 2; c <= last; ++c) {
-      const int64_t sl = c - first < kMaxParts ? sl_k[c - first] : slot_of(c);
-      const float w = c - first < kMaxParts ? w_k[c - first]
-                                            : ex2_approx(__ldcg(t.part_lse + sl * kQRows + qrow) - M);
-      const float4* src = reinterpret_cast<const float4*>(t.part_o + (sl * kQRows + qrow) * kD + ch);
-      float4 v[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q) v[q] = __ldcg(src + q);
-#pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        acc[4 * q] = fmaf(w, v[q].x, acc[4 * q]);
-        acc[4 * q + 1] = fmaf(w, v[q].y, acc[4 * q + 1]);
-        acc[4 * q + 2] = fmaf(w, v[q].z, acc[4 * q + 2]);
-        acc[4 * q + 3] = fmaf(w, v[q].w, acc[4 * q + 3]);
-      }
-    }
-    float lo[32], hi[32];
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      lo[c] = acc[c] * winv;
-      hi[c] = acc[32 + c] * winv;
-    }
-    store_cols32(t, ob, ch, lo);
-    store_cols32(t, ob, ch + 32, hi);
-  }
-  if (a.lse) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
-}
 
 template <int ANCW, bool BF16>
 __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
@@ -498,7 +413,6 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
   const int r = threadIdx.x & 127;              // row within the M-tile = TMEM lane
   const int wq = (threadIdx.x >> 5) & 3;        // warp quarter: TMEM lanes 32*wq..
   const int lane = threadIdx.x & 31;
-  const int wslot = wg * 4 + wq;                // softmax warp 0..7
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(wq * 32) << 16);
   uint8_t* q_tile = smem + kOffQ + wg * 2 * kQHalf;
   const int R = a.group * a.n;
@@ -519,15 +433,22 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     const int P = pi.L - a.n;
     const bool len_ok = pi.L >= a.n;
 
-    // ---- Q row -> shared memory (SW128 K-major), then hand it to the MMA warp
+    // ---- Q row -> shared memory (SW128 K-major), then hand it to the MMA
+    // warp.  Each half of the row (8 chunks) is loaded before any of it is
+    // stored, so the row costs two memory round trips rather than one per
+    // chunk.
+    const bool walk = a.mask_kind == GORGON_MASK_PARENTS;
     {
       const uint4* src = reinterpret_cast<const uint4*>(
           static_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(pi.b) * a.q_sb +
           static_cast<int64_t>(h) * a.q_sh + static_cast<int64_t>(node) * a.q_sn);
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        const uint4 v = row_ok ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(q_tile + (c >> 3) * kQHalf + sw128(r, c & 7)) = v;
+      for (int half = 0; half < 2; ++half) {
+        uint4 qv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) qv[c] = row_ok ? __ldg(src + half * 8 + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(q_tile + half * kQHalf + sw128(r, c)) = qv[c];
       }
       fence_proxy_async_smem();
       tc_fence_before();  // the previous segment's O reads precede the next MMAs
@@ -538,7 +459,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     uint32_t anc[ANCW];
 #pragma unroll
     for (int k = 0; k < ANCW; ++k) anc[k] = 0;
-    if (a.mask_kind == GORGON_MASK_PARENTS) {
+    if (walk) {
       // The warp keeps parents[] in registers (lane l holds entries l, l + 32,
       // ...) and every lane walks its own node's chain through shuffles, so
       // the walk costs one coalesced load instead of a chain of dependent ones.
@@ -547,7 +468,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
 #pragma unroll
       for (int k = 0; k < ANCW; ++k) {
         const int idx = lane + 32 * k;
-        pv[k] = (len_ok && idx < a.n) ? par[idx] : -1;
+        pv[k] = (len_ok && idx < a.n) ? __ldg(par + idx) : -1;
       }
       int cur = (row_ok && len_ok) ? node : -1;
       bool bad = false;
@@ -731,23 +652,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
             make_float4(any ? __uint_as_float(ov[c]) * inv : 0.f, any ? __uint_as_float(ov[c + 1]) * inv : 0.f,
                         any ? __uint_as_float(ov[c + 2]) * inv : 0.f, any ? __uint_as_float(ov[c + 3]) * inv : 0.f);
     }
-    t.part_lse[slot * kQRows + qrow] = lse2;
-    // per-warp arrival count: the warp that completes the set of parts merges
-    // them.  The warp barrier orders every lane's stores before lane 0's
-    // release atomic; the merging warp acquires before reading the others'.
-    __syncwarp();
-    const int64_t first = cta_of(pi.start, T, t.grid);
-    const int64_t last = cta_of(pi.end - 1, T, t.grid);
-    int is_last = 0;
-    if (lane == 0) {
-      __threadfence();
-      const int prev = atomic_add_release_gpu(t.counters + static_cast<int64_t>(p) * 8 + wslot, 1);
-      is_last = prev == static_cast<int>(last - first);
-    }
-    is_last = __shfl_sync(0xffffffffu, is_last, 0);
-    if (!is_last) continue;
-    fence_acquire_gpu();
-    combine_row(t, first, last, pi.start, T, qrow, row_ok, ob, orow);
+    t.part_lse[slot * kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
   }
 }
 
@@ -842,6 +747,93 @@ __global__ void attn_tc_prologue(const TcArgs t) {
   t.tile_start[p] = acc;
 }
 
+// Merges the pieces of every pair that the stream-K schedule cut between
+// CTAs: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M) with M = max_k
+// lse_k (log2 units) and o_k each piece's normalised output.  Grid (pairs,
+// kQRows / kCombineRows): a warp takes one row, a lane one piece's lse (32
+// pieces at a time) and four of the row's columns, so a row costs two memory
+// round trips (the lse values, then every piece's 512-byte row, coalesced, 8
+// pieces in flight per lane).  Pairs that one CTA finished are skipped.
+constexpr int kCombineRows = 8;  // rows per CTA: one per warp
+constexpr int kCombineThreads = 256;
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+__global__ void __launch_bounds__(kCombineThreads) attn_tc_combine(const TcArgs t) {
+  const PairInfo pi = pair_info(t, blockIdx.x);
+  if (pi.end <= pi.start) return;
+  const int64_t T = total_tiles(t);
+  const int64_t first = cta_of(pi.start, T, t.grid);
+  const int64_t last = cta_of(pi.end - 1, T, t.grid);
+  if (first == last) return;
+  const int parts = static_cast<int>(last - first + 1);
+  // a piece's slot: 1 when it is the second pair of its CTA's range
+  auto slot = [&](int64_t c) -> int64_t {
+    return c * 2 + ((c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0);
+  };
+  const AttnArgs& a = t.a;
+  const int R = a.group * a.n;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qrow = blockIdx.y * kCombineRows + warp;
+  const int pr = pi.qg * kQRows + qrow;
+  if (pr >= R) return;
+  const int gq = pr / a.n, node = pr % a.n;
+  const int h = pi.kvh * a.group + gq;
+  const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
+  const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
+                     static_cast<int64_t>(node) * a.o_sn;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = -INFINITY, wsum = 0.f;
+  for (int c0 = 0; c0 < parts; c0 += 32) {
+    // lane j holds piece c0 + j's lse; the group's max rescales what came before
+    const int cj = c0 + lane;
+    const float lj = cj < parts ? __ldcg(t.part_lse + slot(first + cj) * kQRows + qrow) : -INFINITY;
+    const float Mn = fmaxf(M, warp_max(lj));
+    if (Mn == -INFINITY) continue;  // nothing visible yet
+    const float r = ex2_approx(M - Mn);  // 0 while M was -inf
+    acc.x *= r; acc.y *= r; acc.z *= r; acc.w *= r;
+    wsum *= r;
+    M = Mn;
+    const float wj = ex2_approx(lj - M);  // 0 for pieces past the end or with nothing visible
+    const int n_here = min(32, parts - c0);
+    for (int j0 = 0; j0 < n_here; j0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = j0 + j < n_here
+                   ? __ldcg(reinterpret_cast<const float4*>(t.part_o + (slot(first + c0 + j0 + j) * kQRows + qrow) *
+                                                                           kD) + lane)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float w = __shfl_sync(0xffffffffu, wj, (j0 + j) & 31);
+        if (j0 + j < n_here) {
+          wsum += w;
+          acc.x = fmaf(w, v[j].x, acc.x);
+          acc.y = fmaf(w, v[j].y, acc.y);
+          acc.z = fmaf(w, v[j].z, acc.z);
+          acc.w = fmaf(w, v[j].w, acc.w);
+        }
+      }
+    }
+  }
+  if (M == -INFINITY) {  // no visible key in any piece: NaN, like softmax
+    for (int c = lane; c < kD; c += 32) store_as(a.out, a.out_dtype, ob + c, NAN);
+    if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
+    return;
+  }
+  const float winv = 1.f / wsum;
+  store_as(a.out, a.out_dtype, ob + lane * 4, acc.x * winv);
+  store_as(a.out, a.out_dtype, ob + lane * 4 + 1, acc.y * winv);
+  store_as(a.out, a.out_dtype, ob + lane * 4 + 2, acc.z * winv);
+  store_as(a.out, a.out_dtype, ob + lane * 4 + 3, acc.w * winv);
+  if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+}
+
 // ------------------------------------------------------------ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -904,13 +896,12 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t counters, part_o, part_lse, tile_start, total;
+  size_t part_o, part_lse, tile_start, total;
 };
 
 WsLayout ws_layout(const Plan& pl) {
   WsLayout w{};
   size_t off = 0;
-  w.counters = off;   off += align_up(static_cast<size_t>(pl.pairs) * 8 * sizeof(int));
   w.tile_start = off; off += align_up(static_cast<size_t>(pl.pairs + 1) * sizeof(int));
   w.part_lse = off;   off += align_up(static_cast<size_t>(pl.grid) * 2 * kQRows * sizeof(float));
   w.part_o = off;     off += align_up(static_cast<size_t>(pl.grid) * 2 * kQRows * kD * sizeof(float));
@@ -938,7 +929,7 @@ size_t attn_tc_workspace(const AttnArgs& a) { return ws_layout(make_plan(a)).tot
 void attn_tc_plan(const AttnArgs& a, int32_t* splits, int32_t* launches) {
   const Plan pl = make_plan(a);
   *splits = pl.grid;
-  *launches = pl.varlen ? 2 : 1;
+  *launches = 1 + (pl.varlen ? 1 : 0) + (pl.pair_align ? 0 : 1);
 }
 
 int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st) {
@@ -986,15 +977,12 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.pair_align = pl.pair_align;
   t.ab_fmt = dtype == GORGON_BF16 ? 1 : 0;
   char* ws = static_cast<char*>(workspace);
-  t.counters = reinterpret_cast<int*>(ws + w.counters);
   t.tile_start = reinterpret_cast<int*>(ws + w.tile_start);
   t.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   t.part_o = reinterpret_cast<float*>(ws + w.part_o);
   t.out_vec = a.out_dtype == GORGON_BF16 && aligned16(a.out) && a.o_sb % 8 == 0 && a.o_sh % 8 == 0 &&
               a.o_sn % 8 == 0;
-  int rc = check_cuda(cudaMemsetAsync(t.counters, 0, static_cast<size_t>(pl.pairs) * 8 * sizeof(int), st),
-                      "tcgen05 counters reset");
-  if (rc) return rc;
+  int rc = GORGON_OK;
   if (pl.varlen) {
     attn_tc_prologue<<<1, 32, 0, st>>>(t);
     rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
@@ -1006,7 +994,10 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
                   "tcgen05 smem attribute");
   if (rc) return rc;
   kern<<<pl.grid, kThreads, kSmemBytes, st>>>(kmap, vmap, t);
-  return check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
+  rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
+  if (rc || pl.pair_align) return rc;
+  attn_tc_combine<<<dim3(pl.pairs, kQRows / kCombineRows), kCombineThreads, 0, st>>>(t);
+  return check_cuda(cudaGetLastError(), "tcgen05 combine launch");
 }
 
 }  // namespace gorgon
