@@ -25,8 +25,33 @@ def require_cuda(what: str, *tensors: torch.Tensor) -> None:
             raise ValueError(f"{what} must be CUDA tensors.")
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> int:
+    """The cudaStream_t of torch's current stream on `device`, as an int
+    (the raw accessor skips building a Stream object on every call)."""
+    if _raw_stream is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+class _NoSwitch:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_SWITCH = _NoSwitch()
+
+
+def on_device(device: torch.device):
+    """`torch.cuda.device(device)`, or nothing when it is already current."""
+    if device.index is None or torch.cuda.current_device() == device.index:
+        return _NO_SWITCH
+    return torch.cuda.device(device)
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:

@@ -35,6 +35,8 @@
 
 #include <mutex>
 #include <type_traits>
+#include <utility>
+#include <vector>
 
 #include "attn.cuh"
 #include "sm100.cuh"
@@ -911,6 +913,23 @@ WsLayout ws_layout(const Plan& pl) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device)
+// rather than on every launch.
+int ensure_smem_limit(const void* fn) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> done;
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "tcgen05 current device");
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& e : done)
+    if (e.first == fn && e.second == dev) return GORGON_OK;
+  rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+                  "tcgen05 smem attribute");
+  if (!rc) done.emplace_back(fn, dev);
+  return rc;
+}
+
 }  // namespace
 
 bool attn_tc_supported(const AttnArgs& a, int dtype) {
@@ -990,8 +1009,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   }
   auto kern = a.n <= 64 ? (dtype == GORGON_BF16 ? attn_tc_kernel<2, true> : attn_tc_kernel<2, false>)
                         : (dtype == GORGON_BF16 ? attn_tc_kernel<8, true> : attn_tc_kernel<8, false>);
-  rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
-                  "tcgen05 smem attribute");
+  rc = ensure_smem_limit(reinterpret_cast<const void*>(kern));
   if (rc) return rc;
   kern<<<pl.grid, kThreads, kSmemBytes, st>>>(kmap, vmap, t);
   rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");

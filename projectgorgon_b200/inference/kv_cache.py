@@ -15,7 +15,7 @@ from typing import List, Optional, Sequence, Tuple, Union
 import torch
 
 from .. import _abi
-from .._util import require_cuda, stream_ptr
+from .._util import on_device, require_cuda, stream_ptr
 
 PastKV = Tuple[Tuple[torch.Tensor, torch.Tensor], ...]
 
@@ -45,10 +45,7 @@ def _run_trim(p, dev: torch.device, idx: torch.Tensor, lens: torch.Tensor,
     p.src_idx, p.idx_stride_b, p.max_len = idx.data_ptr(), idx.stride(0), idx.shape[1]
     p.lens = lens.data_ptr()
     p.dst_start = dst_start.data_ptr() if dst_start is not None else 0
-    if torch.cuda.current_device() == dev.index:
-        _abi.check(_abi.lib().gorgon_kv_trim(p, stream_ptr(dev)), "gorgon_kv_trim")
-        return
-    with torch.cuda.device(dev):
+    with on_device(dev):
         _abi.check(_abi.lib().gorgon_kv_trim(p, stream_ptr(dev)), "gorgon_kv_trim")
 
 

@@ -15,7 +15,7 @@ from typing import List, Sequence, Tuple, Union
 import torch
 
 from .. import _abi
-from .._util import gorgon_dtype, require_cuda, stream_ptr, workspace
+from .._util import gorgon_dtype, on_device, require_cuda, stream_ptr, workspace
 
 
 @dataclass
@@ -96,7 +96,7 @@ def verify_tree(logits: torch.Tensor, draft: torch.Tensor,
     p.pred, p.accepted_len, p.path = res.pred.data_ptr(), res.accepted_len.data_ptr(), res.path.data_ptr()
     p.bonus, p.best_node, p.hidden_row = res.bonus.data_ptr(), res.best_node.data_ptr(), res.hidden_row.data_ptr()
     lib = _abi.lib()
-    with torch.cuda.device(dev):
+    with on_device(dev):
         nbytes = lib.gorgon_verify_workspace_size(p)
         ws = workspace(nbytes, dev)
         _abi.check(lib.gorgon_verify(p, ws.data_ptr(), ws.numel(), stream_ptr(dev)), "gorgon_verify")

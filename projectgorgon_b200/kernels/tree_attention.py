@@ -24,7 +24,7 @@ from typing import Optional, Sequence, Tuple, Union
 import torch
 
 from .. import _abi
-from .._util import gorgon_dtype, parents_tensor, ptr, require_cuda, stream_ptr, workspace
+from .._util import gorgon_dtype, on_device, parents_tensor, ptr, require_cuda, stream_ptr, workspace
 
 _BACKENDS = {"auto": _abi.BACKEND_AUTO, "simt": _abi.BACKEND_SIMT, "tcgen05": _abi.BACKEND_TCGEN05}
 
@@ -69,7 +69,7 @@ def tree_attention(
                     out_dtype, return_lse, backend, num_splits)
     lib = _abi.lib()
     dev = prep.out.device
-    with torch.cuda.device(dev):
+    with on_device(dev):
         nbytes = lib.gorgon_tree_attn_workspace_size(prep.p)
         ws = workspace(nbytes, dev) if nbytes else None
         _abi.check(lib.gorgon_tree_attn(prep.p, ptr(ws), nbytes, stream_ptr(dev)), "gorgon_tree_attn")
@@ -93,7 +93,7 @@ def tree_attention_plan(q, k, v, tree_mask=None, **kwargs) -> dict:
                     args["backend"], args["num_splits"])
     lib = _abi.lib()
     be, sp, ln = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
-    with torch.cuda.device(prep.out.device):
+    with on_device(prep.out.device):
         _abi.check(lib.gorgon_tree_attn_plan(prep.p, ctypes.byref(be), ctypes.byref(sp), ctypes.byref(ln)),
                    "gorgon_tree_attn_plan")
         nbytes = lib.gorgon_tree_attn_workspace_size(prep.p)

@@ -6,7 +6,7 @@ from typing import Optional, Sequence, Union
 import torch
 
 from .. import _abi
-from .._util import parents_tensor, stream_ptr
+from .._util import on_device, parents_tensor, stream_ptr
 
 
 def build_tree_mask(parents: Union[Sequence[int], torch.Tensor], depth: Optional[int] = None,
@@ -30,7 +30,7 @@ def build_tree_mask(parents: Union[Sequence[int], torch.Tensor], depth: Optional
     B, n = p2.shape
     out = torch.empty((B, n, n), dtype=torch.bool, device=dev)
     d = -1 if depth is None else int(depth)
-    with torch.cuda.device(dev):
+    with on_device(dev):
         _abi.check(_abi.lib().gorgon_tree_mask(p2.data_ptr(), B, n, p2.stride(0), d, out.data_ptr(),
                                                stream_ptr(dev)), "gorgon_tree_mask")
     return out if batched else out[0]
