@@ -46,11 +46,11 @@ from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tre
 NCU_TRAFFIC_BYTES = {
     # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.585 MB read + 3.880 MB written
     ("verify-b16-p8192-n64", "tcgen05"): 553465600,
-    # profiles/verify_kernel_verifier-b32-n64-v128256.md: 533.673 MB read + 3.580 MB written
-    ("verifier-b32-n64-v128256", "verify_kernel"): 537253888,
-    # profiles/kv_trim_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.400 MB read, 0 written)
-    # scaled by 8 to 32 layers
-    ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11196416,
+    # profiles/verify_kernel_verifier-b32-n64-v128256.md: 572.339 MB read + 3.123 MB written
+    ("verifier-b32-n64-v128256", "verify_kernel"): 575461632,
+    # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
+    # 0 written) scaled by 8 to 32 layers
+    ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11108352,
     # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 2181.164 MB read + 7.039 MB written
     ("wide-b8-p32k-n256", "tcgen05"): 2188202976,
 }
