@@ -1,29 +1,41 @@
 // Tensor-core (tcgen05) tree attention for sm_100a.
 //
-// Unit of work: a "pair" = (sequence b, kv head, query group).  A query group
-// packs up to 256 rows of (query head in the GQA group, tree node): row
-// g * n + i.  Those rows share every key/value row of the pair, so each K/V
-// tile is fetched from HBM once and used by two 128-row MMA tiles.
+// Unit of work: MT 128-row M-tiles of one (sequence b, kv head) — a "unit".
+// The packed query rows of a (b, kv head) are (query head in the GQA group,
+// tree node): row g * n + i; a unit takes MT * 128 consecutive packed rows.
+// Those rows share every key/value row of the sequence, so each K/V tile a
+// CTA fetches feeds all MT of its MMA tiles.  Two shapes, chosen per launch:
 //
-// Schedule: a grid of at most one CTA per SM.  When pairs roughly fill the
-// SMs, each CTA takes whole pairs.  Otherwise (stream-K) the pair-major list
-// of 64-row key/value tiles is split into equal contiguous ranges: a pair
-// that falls inside one CTA is finished there; a pair cut between CTAs leaves
-// normalised partials plus log-sum-exp in the workspace, and attn_tc_combine,
-// launched right after, merges them with one warp per row.
+//   MT = 2: 256 rows per unit, 64-row K/V tiles, 384 threads (two softmax
+//           warpgroups), 5-stage K and V rings.
+//   MT = 1: 128 rows per unit, 128-row K/V tiles, 256 threads (one softmax
+//           warpgroup), 3-stage rings.  Q.K^T runs at N = 128 (the tensor
+//           pipe's full rate; N = 64 takes ~57 cycles per K step for 32 of
+//           math), the softmax thread keeps a 128-column row in registers
+//           (255 per thread at 256 threads), and the two units of a 256-row
+//           group run on neighbouring CTAs that share K/V through L2.
 //
-// Warp roles (384 threads):
-//   warp 0       TMA producer for K tiles (two 64-column SW128 boxes), 5-stage ring
-//   warp 3       TMA producer for V tiles, its own 5-stage ring
+// Schedule: a grid of at most one CTA per SM.  When whole units roughly fill
+// the SMs, CTA c takes units c, c + grid, ... (so the units that share K/V run
+// at the same time).  Otherwise (stream-K) the unit-major list of K/V tiles
+// is split into equal contiguous ranges: a unit that falls inside one CTA is
+// finished there; a unit cut between CTAs leaves normalised partials plus
+// log-sum-exp in the workspace, and attn_tc_combine, launched right after,
+// merges them with one warp per row.
+//
+// Warp roles:
+//   warp 0       TMA producer for K tiles (two 64-column SW128 boxes)
+//   warp 3       TMA producer for V tiles, its own ring
 //   warp 1       Q.K^T issuer (one thread): S = Q K^T into TMEM
 //   warp 2       P.V issuer (one thread): O += P V with P read from TMEM; the
 //                warp also allocates and releases TMEM
 //   warps 4-7    softmax + epilogue of M-tile 0 (TMEM lanes 0-127)
-//   warps 8-11   softmax + epilogue of M-tile 1
-// TMEM (512 columns): S double-buffered (2 buffers x 2 M-tiles x 64 columns),
-// O (2 M-tiles x 128 columns).  P (bf16, two per 32-bit column) overwrites the
-// first 32 columns of its own S buffer and is the TMEM A operand of P.V.
-// A K stage is released as soon as its Q.K^T completes, a V stage after P.V.
+//   warps 8-11   (MT = 2) softmax + epilogue of M-tile 1
+// TMEM (512 columns): S double-buffered (2 buffers x MT M-tiles x BN
+// columns, 256 in all) and O (MT x 128 columns).  P (16-bit pairs)
+// overwrites the first BN / 2 columns of its own S buffer and is the TMEM A
+// operand of P.V.  A K stage is released as soon as its Q.K^T completes, a V
+// stage after P.V.
 //
 // Softmax per row is owned by one thread (TMEM lane = row), so row max and
 // sum need no shuffles.  Rescaling of O is lazy: the running max only moves
@@ -49,58 +61,63 @@ namespace {
 using namespace sm100;
 
 constexpr int kBM = 128;              // rows per MMA tile
-constexpr int kQRows = 2 * kBM;       // packed query rows per pair
-constexpr int kBN = 64;               // key/value rows per tile
 constexpr int kD = 128;               // head_dim
-constexpr int kStages = 5;             // per ring (K and V)
-constexpr int kThreads = 384;
 constexpr long long kWaitLimitCycles = 4000000000ll;  // about 2 s at the boost clock
-
-// shared memory layout (bytes from a 1024-aligned base)
 constexpr uint32_t kQHalf = kBM * 128;                 // 128 rows x 64 cols bf16 = 16 KB
-constexpr uint32_t kKVHalf = kBN * 128;                // 64 rows x 64 cols = 8 KB
-constexpr uint32_t kTileBytes = 2 * kKVHalf;           // one K or V tile, two halves
 constexpr uint32_t kOffQ = 0;                          // [mtile][half]
-constexpr uint32_t kOffK = kOffQ + 4 * kQHalf;         // [stage][half]
-constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;  // + alignment slack
-
-// TMEM columns
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0;    // + (buf * 2 + mtile) * 64
+constexpr uint32_t kColS = 0;    // + (buf * MT + mtile) * BN
 constexpr uint32_t kColO = 256;  // + mtile * 128
+
+// The constants that follow from MT, the 128-row M-tiles per CTA.
+template <int MT>
+struct Cfg {
+  static_assert(MT == 1 || MT == 2, "one or two M-tiles per CTA");
+  static constexpr int kQRows = MT * kBM;          // packed query rows per unit
+  static constexpr int kBN = MT == 2 ? 64 : 128;   // key/value rows per tile
+  static constexpr int kStages = MT == 2 ? 5 : 3;  // per ring (K and V)
+  static constexpr int kThreads = 128 + MT * 128;
+  static constexpr uint32_t kKVHalf = kBN * 128;   // BN rows x 64 cols bf16
+  static constexpr uint32_t kTileBytes = 2 * kKVHalf;
+  static constexpr uint32_t kOffK = kOffQ + MT * 2 * kQHalf;  // [stage][half]
+  static constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
+  static constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
+  static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 232448, "shared memory per block");
+  static_assert(2 * MT * kBN <= kColO, "S buffers below O");
+};
 
 struct TcArgs {
   AttnArgs a;
   int varlen;
-  int qgroups;        // query groups per (b, kv head)
-  int pairs;          // batch * hkv * qgroups
-  int tiles_per_pair; // uniform lengths only
+  int qgroups;        // units per (b, kv head)
+  int pairs;          // units: batch * hkv * qgroups
+  int tiles_per_pair; // tiles per unit (uniform lengths only)
   int grid;
-  int pair_align;     // CTA ranges hold whole pairs (no partials to merge)
+  int pair_align;     // whole units per CTA, strided by the grid (no partials to merge)
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // bf16 output with 16-byte aligned rows
-  float* part_o;      // [grid * 2][256][128]
-  float* part_lse;    // [grid * 2][256]
-  int* tile_start;    // varlen: [pairs + 1] tile prefix (written by attn_tc_prologue)
+  float* part_o;      // [grid * 2][rows per unit][128]
+  float* part_lse;    // [grid * 2][rows per unit]
+  int* tile_start;    // varlen: [units + 1] tile prefix (written by attn_tc_prologue)
 };
 
+template <int MT>
 struct Barriers {
-  uint64_t k_full[kStages];
-  uint64_t k_empty[kStages];
-  uint64_t v_full[kStages];
-  uint64_t v_empty[kStages];
+  uint64_t k_full[Cfg<MT>::kStages];
+  uint64_t k_empty[Cfg<MT>::kStages];
+  uint64_t v_full[Cfg<MT>::kStages];
+  uint64_t v_empty[Cfg<MT>::kStages];
   uint64_t q_full;
-  // per (S buffer, M-tile): index buf * 2 + mtile
-  uint64_t s_full[4];
-  uint64_t p_full[4];
-  uint64_t p_free[4];  // P.V of the tile in this buffer has completed
-  uint64_t drain[2];   // all MMAs of the Q.K^T / P.V issuer complete
+  // per (S buffer, M-tile): index buf * MT + mtile
+  uint64_t s_full[2 * MT];
+  uint64_t p_full[2 * MT];
+  uint64_t p_free[2 * MT];  // P.V of the tile in this buffer has completed
+  uint64_t drain[2];        // all MMAs of the Q.K^T / P.V issuer complete
   uint32_t tmem_base;
   int abort;
 };
-static_assert(sizeof(Barriers) <= 512, "barrier block");
+static_assert(sizeof(Barriers<2>) <= 512 && sizeof(Barriers<1>) <= 512, "barrier block");
 
 // ------------------------------------------------------------ schedule
 __device__ __forceinline__ int64_t total_tiles(const TcArgs& t) {
@@ -149,6 +166,36 @@ __device__ __forceinline__ PairInfo pair_info(const TcArgs& t, int p) {
   return pi;
 }
 
+// The segments (the tiles of one unit each) a CTA works through, the same
+// sequence for every role: whole units blockIdx.x, blockIdx.x + grid, ...
+// when t.pair_align, else the pieces of units inside the CTA's tile range
+// [g0, g1) (stream-K).
+struct Segments {
+  int64_t g0, g1;
+  int unit;
+  __device__ Segments(int64_t r0, int64_t r1) : g0(r0), g1(r1), unit(blockIdx.x) {}
+  __device__ bool next(const TcArgs& t, int64_t& g, int64_t& e, PairInfo& pi) {
+    if (t.pair_align) {
+      while (unit < t.pairs) {
+        pi = pair_info(t, unit);
+        unit += t.grid;
+        if (pi.end > pi.start) {
+          g = pi.start;
+          e = pi.end;
+          return true;
+        }
+      }
+      return false;
+    }
+    if (g0 >= g1) return false;
+    pi = pair_info(t, pair_of(t, g0));
+    g = g0;
+    e = min(g1, pi.end);
+    g0 = e;
+    return true;
+  }
+};
+
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` in an SW128 K-major
 // tile whose rows are 128 bytes.
 __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
@@ -189,104 +236,110 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // ------------------------------------------------------------ roles
-// Streams one operand (K when is_v == 0, else V) of every tile in [g0, g1)
-// through its ring.
-__device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem, Barriers* bars, int64_t g0,
+// Streams one operand (K when is_v == 0, else V) of every tile of the CTA's
+// segments through its ring.
+template <int MT>
+__device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem, Barriers<MT>* bars, int64_t g0,
                          int64_t g1, int is_v) {
+  using C = Cfg<MT>;
   volatile int* abort = &bars->abort;
   uint64_t* full = is_v ? bars->v_full : bars->k_full;
   uint64_t* empty = is_v ? bars->v_empty : bars->k_empty;
-  uint8_t* ring = smem + (is_v ? kOffV : kOffK);
+  uint8_t* ring = smem + (is_v ? C::kOffV : C::kOffK);
   int64_t issued = 0;
-  int cur_pair = -1;
-  PairInfo pi{};
-  // With one query group per (sequence, kv head) K/V are read once: keep them
-  // from pushing the partial results out of L2.  With several, the groups'
-  // CTAs run side by side over the same K/V, and the later ones should find
-  // it in L2.
+  // With one unit per (sequence, kv head) K/V are read once: keep them from
+  // pushing the partial results out of L2.  With several, the units' CTAs run
+  // side by side over the same K/V, and the later ones should find it in L2.
   const uint64_t policy = t.qgroups > 1 ? l2_policy_evict_last() : l2_policy_evict_first();
-  for (int64_t g = g0; g < g1; ++g) {
-    const int p = pair_of(t, g);
-    if (p != cur_pair) {
-      cur_pair = p;
-      pi = pair_info(t, p);
+  Segments sg(g0, g1);
+  int64_t g, e;
+  PairInfo pi;
+  bool ok = true;
+  while (ok && sg.next(t, g, e, pi)) {
+    for (; g < e; ++g) {
+      const int tile = static_cast<int>(g - pi.start);
+      const int stage = static_cast<int>(issued % C::kStages);
+      const uint32_t ph = static_cast<uint32_t>(issued / C::kStages) & 1u;
+      if (!bounded_wait(&empty[stage], ph ^ 1u, abort)) {
+        ok = false;
+        break;
+      }
+      mbar_arrive_expect_tx(&full[stage], C::kTileBytes);
+      uint8_t* st = ring + stage * C::kTileBytes;
+      const int row = tile * C::kBN;
+      if (t.varlen) {
+        const int r = pi.row0 + row;
+        tma_load_3d_hint(st, map, &full[stage], 0, pi.kvh, r, policy);
+        tma_load_3d_hint(st + C::kKVHalf, map, &full[stage], 64, pi.kvh, r, policy);
+      } else {
+        tma_load_4d_hint(st, map, &full[stage], 0, row, pi.kvh, pi.b, policy);
+        tma_load_4d_hint(st + C::kKVHalf, map, &full[stage], 64, row, pi.kvh, pi.b, policy);
+      }
+      ++issued;
     }
-    const int tile = static_cast<int>(g - pi.start);
-    const int stage = static_cast<int>(issued % kStages);
-    const uint32_t ph = static_cast<uint32_t>(issued / kStages) & 1u;
-    if (!bounded_wait(&empty[stage], ph ^ 1u, abort)) break;
-    mbar_arrive_expect_tx(&full[stage], kTileBytes);
-    uint8_t* st = ring + stage * kTileBytes;
-    const int row = tile * kBN;
-    if (t.varlen) {
-      const int r = pi.row0 + row;
-      tma_load_3d_hint(st, map, &full[stage], 0, pi.kvh, r, policy);
-      tma_load_3d_hint(st + kKVHalf, map, &full[stage], 64, pi.kvh, r, policy);
-    } else {
-      tma_load_4d_hint(st, map, &full[stage], 0, row, pi.kvh, pi.b, policy);
-      tma_load_4d_hint(st + kKVHalf, map, &full[stage], 64, row, pi.kvh, pi.b, policy);
-    }
-    ++issued;
   }
   // Every issued load must land before the CTA leaves.
-  for (int64_t k = (issued > kStages ? issued - kStages : 0); k < issued; ++k)
-    drain_wait(&full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u);
+  for (int64_t k = (issued > C::kStages ? issued - C::kStages : 0); k < issued; ++k)
+    drain_wait(&full[k % C::kStages], static_cast<uint32_t>(k / C::kStages) & 1u);
 }
 
 // Ring position of a tile counter, advanced without divisions.
+template <int N>
 struct Ring {
   uint32_t stage = 0, phase = 0;
   __device__ __forceinline__ void next() {
-    if (++stage == kStages) {
+    if (++stage == N) {
       stage = 0;
       phase ^= 1u;
     }
   }
 };
 
-// The MMA issuer keeps every operand descriptor in registers and only adds
+// The MMA issuers keep every operand descriptor in registers and only add
 // constant offsets (in the descriptor's 16-byte address units) per K step.
 struct MmaDescs {
-  uint64_t q[2][2];  // [mtile][d half], SW128 K-major, SBO 1 KB
-  uint64_t k0;       // K ring stage 0, half 0
-  uint64_t v0;       // V ring stage 0: MN-major, LBO 8 KB (d halves), SBO 1 KB
+  uint64_t q0;  // Q M-tile 0, d half 0 ([mtile][half] at 16 KB steps), SW128 K-major, SBO 1 KB
+  uint64_t k0;  // K ring stage 0, half 0
+  uint64_t v0;  // V ring stage 0: MN-major, LBO = one d half of a tile, SBO 1 KB
   uint32_t idesc_qk, idesc_pv;
 };
 
-// S_mt = Q_mt K^T of one tile into S buffer `buf`.
+// S_mt = Q_mt K^T of one tile into S buffer `buf` (M 128, N BN, K 128).
+template <int MT>
 __device__ __forceinline__ void issue_qk(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf, int mt) {
-  const uint64_t kst = md.k0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
-  const uint32_t d_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
+  using C = Cfg<MT>;
+  const uint64_t kst = md.k0 + static_cast<uint64_t>(stage * (C::kTileBytes >> 4));
+  const uint32_t d_tmem = tmem + kColS + (buf * MT + mt) * C::kBN;
 #pragma unroll
   for (int ks = 0; ks < kD / 16; ++ks) {
-    const uint64_t a = md.q[mt][ks >> 2] + static_cast<uint64_t>((ks & 3) * 2);
-    const uint64_t b = kst + static_cast<uint64_t>((ks >> 2) * (kKVHalf >> 4) + (ks & 3) * 2);
+    const uint64_t a = md.q0 + static_cast<uint64_t>((mt * 2 + (ks >> 2)) * (kQHalf >> 4) + (ks & 3) * 2);
+    const uint64_t b = kst + static_cast<uint64_t>((ks >> 2) * (C::kKVHalf >> 4) + (ks & 3) * 2);
     umma_f16_ss(d_tmem, a, b, md.idesc_qk, ks > 0 ? 1u : 0u);
   }
 }
 
-// O_mt += P_mt (TMEM, over S buffer `buf`) * V (smem stage).
+// O_mt += P_mt (TMEM, over S buffer `buf`) * V (smem stage): M 128, N 128, K BN.
+template <int MT>
 __device__ __forceinline__ void issue_pv(const MmaDescs& md, uint32_t tmem, uint32_t stage, uint32_t buf, int mt,
                                          uint32_t first) {
-  const uint64_t vst = md.v0 + static_cast<uint64_t>(stage * (kTileBytes >> 4));
+  using C = Cfg<MT>;
+  const uint64_t vst = md.v0 + static_cast<uint64_t>(stage * (C::kTileBytes >> 4));
   const uint32_t d_tmem = tmem + kColO + mt * kD;
-  const uint32_t p_tmem = tmem + kColS + (buf * 2 + mt) * kBN;
+  const uint32_t p_tmem = tmem + kColS + (buf * MT + mt) * C::kBN;
 #pragma unroll
-  for (int ks = 0; ks < kBN / 16; ++ks) {
+  for (int ks = 0; ks < C::kBN / 16; ++ks) {
     umma_f16_ts(d_tmem, p_tmem + ks * 8, vst + static_cast<uint64_t>(ks * (2048 >> 4)), md.idesc_pv,
                 (ks > 0 || !first) ? 1u : 0u);
   }
 }
 
+template <int MT>
 __device__ __forceinline__ void make_descs(const TcArgs& t, uint8_t* smem, MmaDescs& md) {
-  const uint32_t q_base = smem_u32(smem + kOffQ);
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) md.q[mt][h] = umma_desc_sw128(q_base + (mt * 2 + h) * kQHalf, 16, 1024);
-  md.k0 = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
-  md.v0 = umma_desc_sw128(smem_u32(smem + kOffV), kKVHalf, 1024);
-  md.idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, kBN, 0, 0);
+  using C = Cfg<MT>;
+  md.q0 = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+  md.k0 = umma_desc_sw128(smem_u32(smem + C::kOffK), 16, 1024);
+  md.v0 = umma_desc_sw128(smem_u32(smem + C::kOffV), C::kKVHalf, 1024);
+  md.idesc_qk = umma_idesc_f16(t.ab_fmt, kBM, C::kBN, 0, 0);
   md.idesc_pv = umma_idesc_f16(t.ab_fmt, kBM, kD, 0, 1);
 }
 
@@ -295,76 +348,81 @@ __device__ __forceinline__ void make_descs(const TcArgs& t, uint8_t* smem, MmaDe
 // bookkeeping.  S buffer i & 1 doubles as P's storage, so Q.K^T(i) waits for
 // P.V(i - 2) to complete before overwriting it.  Both spin on their barriers
 // (they have nothing else to do) to start the moment their inputs land.
-__device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0, int64_t g1) {
+template <int MT>
+__device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, uint32_t tmem, int64_t g0,
+                          int64_t g1) {
   volatile int* abort = &bars->abort;
   MmaDescs md;
-  make_descs(t, smem, md);
-  Ring kr;
+  make_descs<MT>(t, smem, md);
+  Ring<Cfg<MT>::kStages> kr;
   uint32_t i = 0, seg = 0;
-  for (int64_t g = g0; g < g1; ++seg) {
-    const PairInfo pi = pair_info(t, pair_of(t, g));
-    const uint32_t n_tiles = static_cast<uint32_t>(min(g1, pi.end) - g);
+  Segments sg(g0, g1);
+  int64_t g, e;
+  PairInfo pi;
+  bool ok = true;
+  while (ok && sg.next(t, g, e, pi)) {
+    const uint32_t n_tiles = static_cast<uint32_t>(e - g);
     if (!spin_wait(&bars->q_full, seg & 1u, abort)) break;
-    bool ok = true;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
       if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort)) {
         ok = false;
         break;
       }
-      // per M-tile: each softmax warpgroup starts as soon as its own half lands
-      for (int mt = 0; mt < 2 && ok; ++mt) {
-        const uint32_t bi = (i & 1u) * 2 + mt;
+      // per M-tile: each softmax warpgroup starts as soon as its own S lands
+      for (int mt = 0; mt < MT && ok; ++mt) {
+        const uint32_t bi = (i & 1u) * MT + mt;
         if (i >= 2 && !spin_wait(&bars->p_free[bi], ((i - 2) >> 1) & 1u, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        issue_qk(md, tmem, kr.stage, i & 1u, mt);
+        issue_qk<MT>(md, tmem, kr.stage, i & 1u, mt);
         umma_commit(&bars->s_full[bi]);
       }
       if (!ok) break;
       umma_commit(&bars->k_empty[kr.stage]);
       kr.next();
     }
-    if (!ok) break;
-    g += n_tiles;
+    ++seg;
   }
   umma_commit(&bars->drain[0]);
   drain_wait(&bars->drain[0], 0);
 }
 
-__device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0, int64_t g1) {
+template <int MT>
+__device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, uint32_t tmem, int64_t g0,
+                          int64_t g1) {
   volatile int* abort = &bars->abort;
   MmaDescs md;
-  make_descs(t, smem, md);
-  Ring vr;
+  make_descs<MT>(t, smem, md);
+  Ring<Cfg<MT>::kStages> vr;
   uint32_t i = 0;
-  for (int64_t g = g0; g < g1;) {
-    const PairInfo pi = pair_info(t, pair_of(t, g));
-    const uint32_t n_tiles = static_cast<uint32_t>(min(g1, pi.end) - g);
-    bool ok = true;
+  Segments sg(g0, g1);
+  int64_t g, e;
+  PairInfo pi;
+  bool ok = true;
+  while (ok && sg.next(t, g, e, pi)) {
+    const uint32_t n_tiles = static_cast<uint32_t>(e - g);
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
       const uint32_t buf = i & 1u;
       if (!spin_wait(&bars->v_full[vr.stage], vr.phase, abort)) {
         ok = false;
         break;
       }
-      for (int mt = 0; mt < 2 && ok; ++mt) {
-        const uint32_t bi = buf * 2 + mt;
+      for (int mt = 0; mt < MT && ok; ++mt) {
+        const uint32_t bi = buf * MT + mt;
         if (!spin_wait(&bars->p_full[bi], (i >> 1) & 1u, abort)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        issue_pv(md, tmem, vr.stage, buf, mt, j == 0);
+        issue_pv<MT>(md, tmem, vr.stage, buf, mt, j == 0);
         umma_commit(&bars->p_free[bi]);
       }
       if (!ok) break;
       umma_commit(&bars->v_empty[vr.stage]);
       vr.next();
     }
-    if (!ok) break;
-    g += n_tiles;
   }
   umma_commit(&bars->drain[1]);
   drain_wait(&bars->drain[1], 0);
@@ -405,13 +463,14 @@ __device__ __forceinline__ void store_cols32(const TcArgs& t, int64_t ob, int co
   }
 }
 
-
-template <int ANCW, bool BF16>
-__device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars, uint32_t tmem, int64_t g0,
-                                 int64_t g1, int64_t T, int cta) {
+template <int MT, int ANCW, bool BF16>
+__device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, uint32_t tmem, int64_t g0,
+                                 int64_t g1, int cta) {
+  using C = Cfg<MT>;
+  constexpr int kBN = C::kBN;
   const AttnArgs& a = t.a;
   volatile int* abort = &bars->abort;
-  const int wg = (threadIdx.x >> 7) - 1;       // 0 or 1: M-tile
+  const int wg = (threadIdx.x >> 7) - 1;       // M-tile: 0 .. MT - 1
   const int r = threadIdx.x & 127;              // row within the M-tile = TMEM lane
   const int wq = (threadIdx.x >> 5) & 3;        // warp quarter: TMEM lanes 32*wq..
   const int lane = threadIdx.x & 31;
@@ -420,14 +479,15 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
   const int R = a.group * a.n;
   const float sl2 = a.scale_log2;
   constexpr bool ab_bf16 = BF16;  // P's 16-bit type (that of Q, K and V)
-  const int qrow = wg * kBM + r;                // row within the pair's 256
+  const int qrow = wg * kBM + r;                // row within the unit
   int64_t i = 0;
-  for (int64_t g = g0; g < g1;) {
-    const int p = pair_of(t, g);
-    const PairInfo pi = pair_info(t, p);
-    const int64_t e = min(g1, pi.end);
+  Segments sg(g0, g1);
+  int64_t g, e;
+  PairInfo pi;
+  while (sg.next(t, g, e, pi)) {
+    const bool whole = g == pi.start && e == pi.end;
     const int64_t i_first = i;
-    const int pr = pi.qg * kQRows + qrow;  // packed row
+    const int pr = pi.qg * C::kQRows + qrow;  // packed row
     const bool row_ok = pr < R;
     const int gq = row_ok ? pr / a.n : 0;
     const int node = row_ok ? pr % a.n : 0;
@@ -507,26 +567,26 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
     float m_used = -INFINITY, l = 0.f;
     // One tile of this row: S -> P against the lazy running max.  Masked
     // tiles reach the tree rows or the sequence end and hide the columns this
-    // row may not see; the others (all but the last one or two of a pair) run
+    // row may not see; the others (all but the last one or two of a unit) run
     // a loop without that code, which keeps the hot loop's register
     // allocation and schedule tight.
     auto tile = [&](auto mask_tag) -> bool {
       constexpr bool kMask = decltype(mask_tag)::value;
       const uint32_t buf = static_cast<uint32_t>(i & 1);
-      if (!warp_wait(&bars->s_full[buf * 2 + wg], static_cast<uint32_t>(i >> 1) & 1u, abort)) return false;
+      const uint32_t bi = buf * MT + wg;
+      if (!warp_wait(&bars->s_full[bi], static_cast<uint32_t>(i >> 1) & 1u, abort)) return false;
       tc_fence_after();
+      const uint32_t s_addr = lane_base + kColS + bi * kBN;
       float x[kBN];
       {
-        uint32_t r0[32], r1[32];
-        const uint32_t s_addr = lane_base + kColS + (buf * 2 + wg) * kBN;
-        tmem_ld32(s_addr, r0);
-        tmem_ld32(s_addr + 32, r1);
+        uint32_t rr[kBN / 32][32];
+#pragma unroll
+        for (int q = 0; q < kBN / 32; ++q) tmem_ld32(s_addr + 32 * q, rr[q]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          x[c] = __uint_as_float(r0[c]);
-          x[32 + c] = __uint_as_float(r1[c]);
-        }
+        for (int q = 0; q < kBN / 32; ++q)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) x[32 * q + c] = __uint_as_float(rr[q][c]);
       }
       if (kMask) {
         const int c0 = static_cast<int>(g - pi.start) * kBN;
@@ -584,7 +644,8 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
-        if (!warp_wait(&bars->p_free[(pv & 1) * 2 + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort)) return false;
+        if (!warp_wait(&bars->p_free[(pv & 1) * MT + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort))
+          return false;
         tc_fence_after();
         const uint32_t o_addr = lane_base + kColO + wg * kD;
 #pragma unroll
@@ -598,15 +659,21 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
         }
         tmem_wait_st();
       }
-      // P row (bf16 pairs) -> the first 32 columns of this tile's S buffer
-      tmem_st32(lane_base + kColS + (buf * 2 + wg) * kBN, packed);
+      // P row (16-bit pairs) -> the first BN / 2 columns of this tile's S buffer
+#pragma unroll
+      for (int q = 0; q < kBN / 64; ++q) {
+        uint32_t pq[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pq[c] = packed[32 * q + c];
+        tmem_st32(s_addr + 32 * q, pq);
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->p_full[buf * 2 + wg]);
+      if (lane == 0) mbar_arrive(&bars->p_full[bi]);
       return true;
     };
-    // tiles whose 64 columns all lie in the prefix before the tree rows
+    // tiles whose BN columns all lie in the prefix before the tree rows
     const int64_t plain_end = len_ok ? pi.start + P / kBN : pi.start;
     for (; g < min(e, plain_end); ++g, ++i)
       if (!tile(std::integral_constant<bool, false>())) return;
@@ -615,9 +682,8 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
 
     // ---- epilogue: O / l for this row, once the last P.V has landed
     const int64_t lastv = i - 1;
-    if (!warp_wait(&bars->p_free[(lastv & 1) * 2 + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort)) return;
+    if (!warp_wait(&bars->p_free[(lastv & 1) * MT + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort)) return;
     tc_fence_after();
-    const bool whole = pi.start >= g0 && pi.end <= g1;
     const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
     const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
                        static_cast<int64_t>(node) * a.o_sn;
@@ -638,10 +704,10 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
       if (row_ok && a.lse) a.lse[orow] = lse2 * 0.6931471805599453f;
       continue;
     }
-    // partial: slot 0 when this piece of the pair starts the CTA's range, else slot 1
+    // partial: slot 0 when this piece of the unit starts the CTA's range, else slot 1
     const int which = (pi.start <= g0) ? 0 : 1;
     const int64_t slot = static_cast<int64_t>(cta) * 2 + which;
-    float* po = t.part_o + (slot * kQRows + qrow) * kD;
+    float* po = t.part_o + (slot * C::kQRows + qrow) * kD;
     const bool any = l > 0.f;
 #pragma unroll
     for (int ch = 0; ch < kD / 32; ++ch) {
@@ -654,29 +720,30 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers* bars,
             make_float4(any ? __uint_as_float(ov[c]) * inv : 0.f, any ? __uint_as_float(ov[c + 1]) * inv : 0.f,
                         any ? __uint_as_float(ov[c + 2]) * inv : 0.f, any ? __uint_as_float(ov[c + 3]) * inv : 0.f);
     }
-    t.part_lse[slot * kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
+    t.part_lse[slot * C::kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
   }
 }
 
-template <int ANCW, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MT, int ANCW, bool BF16>
+__global__ void __launch_bounds__(Cfg<MT>::kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                const __grid_constant__ TcArgs t) {
+  using C = Cfg<MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kOffBar);
+  Barriers<MT>* bars = reinterpret_cast<Barriers<MT>*>(smem + C::kOffBar);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
       mbar_init(&bars->k_empty[s], 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
-    mbar_init(&bars->q_full, 8);
-    for (int b = 0; b < 4; ++b) {
+    mbar_init(&bars->q_full, 4 * MT);  // every softmax warp
+    for (int b = 0; b < 2 * MT; ++b) {
       mbar_init(&bars->s_full[b], 1);
       mbar_init(&bars->p_full[b], 4);  // the four warps of one softmax warpgroup
       mbar_init(&bars->p_free[b], 1);
@@ -699,28 +766,28 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  const int64_t T = total_tiles(t);
-  const int64_t G = t.grid;
-  int64_t g0, g1;
+  int64_t g0 = 0, g1 = 0;
+  bool work;
   if (t.pair_align) {
-    g0 = pair_start(t, static_cast<int>(static_cast<int64_t>(blockIdx.x) * t.pairs / G));
-    g1 = pair_start(t, static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * t.pairs / G));
+    work = static_cast<int>(blockIdx.x) < t.pairs;
   } else {
-    g0 = range_start(blockIdx.x, T, G);
-    g1 = range_start(blockIdx.x + 1, T, G);
+    const int64_t T = total_tiles(t);
+    g0 = range_start(blockIdx.x, T, t.grid);
+    g1 = range_start(blockIdx.x + 1, T, t.grid);
+    work = g0 < g1;
   }
 
-  if (g0 < g1) {
+  if (work) {
     if (warp == 0) {
-      if (lane == 0) producer(t, &kmap, smem, bars, g0, g1, 0);
+      if (lane == 0) producer<MT>(t, &kmap, smem, bars, g0, g1, 0);
     } else if (warp == 3) {
-      if (lane == 0) producer(t, &vmap, smem, bars, g0, g1, 1);
+      if (lane == 0) producer<MT>(t, &vmap, smem, bars, g0, g1, 1);
     } else if (warp == 1) {
-      if (lane == 0) qk_issuer(t, smem, bars, tmem, g0, g1);
+      if (lane == 0) qk_issuer<MT>(t, smem, bars, tmem, g0, g1);
     } else if (warp == 2) {
-      if (lane == 0) pv_issuer(t, smem, bars, tmem, g0, g1);
+      if (lane == 0) pv_issuer<MT>(t, smem, bars, tmem, g0, g1);
     } else if (warp >= 4) {
-      softmax_epilogue<ANCW, BF16>(t, smem, bars, tmem, g0, g1, T, blockIdx.x);
+      softmax_epilogue<MT, ANCW, BF16>(t, smem, bars, tmem, g0, g1, blockIdx.x);
     }
   }
   __syncwarp();  // role warps ran their loop on lane 0: reconverge before the CTA barrier
@@ -733,9 +800,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   }
 }
 
-// Varlen schedule: tile prefix over pairs (one thread; pairs are few).
+// Varlen schedule: tile prefix over units (one thread; units are few).
+template <int MT>
 __global__ void attn_tc_prologue(const TcArgs t) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  constexpr int kBN = Cfg<MT>::kBN;
   int acc = 0;
   int p = 0;
   for (int b = 0; b < t.a.batch; ++b) {
@@ -749,13 +818,14 @@ __global__ void attn_tc_prologue(const TcArgs t) {
   t.tile_start[p] = acc;
 }
 
-// Merges the pieces of every pair that the stream-K schedule cut between
+// Merges the pieces of every unit that the stream-K schedule cut between
 // CTAs: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M) with M = max_k
-// lse_k (log2 units) and o_k each piece's normalised output.  Grid (pairs,
-// kQRows / kCombineRows): a warp takes one row, a lane one piece's lse (32
-// pieces at a time) and four of the row's columns, so a row costs two memory
-// round trips (the lse values, then every piece's 512-byte row, coalesced, 8
-// pieces in flight per lane).  Pairs that one CTA finished are skipped.
+// lse_k (log2 units) and o_k each piece's normalised output.  Grid (units,
+// rows per unit / kCombineRows): a warp takes one row, a lane one piece's lse
+// (32 pieces at a time) and four of the row's columns, so a row costs two
+// memory round trips (the lse values, then every piece's 512-byte row,
+// coalesced, 8 pieces in flight per lane).  Units that one CTA finished are
+// skipped.
 constexpr int kCombineRows = 8;  // rows per CTA: one per warp
 constexpr int kCombineThreads = 256;
 
@@ -765,7 +835,9 @@ __device__ __forceinline__ float warp_max(float x) {
   return x;
 }
 
+template <int MT>
 __global__ void __launch_bounds__(kCombineThreads) attn_tc_combine(const TcArgs t) {
+  constexpr int kQRows = Cfg<MT>::kQRows;
   const PairInfo pi = pair_info(t, blockIdx.x);
   if (pi.end <= pi.start) return;
   const int64_t T = total_tiles(t);
@@ -773,7 +845,7 @@ __global__ void __launch_bounds__(kCombineThreads) attn_tc_combine(const TcArgs 
   const int64_t last = cta_of(pi.end - 1, T, t.grid);
   if (first == last) return;
   const int parts = static_cast<int>(last - first + 1);
-  // a piece's slot: 1 when it is the second pair of its CTA's range
+  // a piece's slot: 1 when it is the second unit of its CTA's range
   auto slot = [&](int64_t c) -> int64_t {
     return c * 2 + ((c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0);
   };
@@ -855,14 +927,29 @@ EncodeTiledFn encode_fn() {
 }
 
 struct Plan {
+  int mt;  // 128-row M-tiles per CTA
   int qgroups, pairs, tiles_per_pair, grid;
   bool varlen, pair_align;
 };
 
-Plan make_plan(const AttnArgs& a) {
+// Two M-tiles per CTA unless the 256-row units would leave most SMs idle.
+// Measured on B200 (bf16, 32 q / 8 kv heads, 64-node trees): with whole units
+// filling the GPU, MT = 2 is the faster shape (16 x 8192 prefix: 158 us
+// against 184 for MT = 1; 256-node trees over 32k: 1142 against 1351 us;
+// ragged 16 x 1k-8k: 172 against 209 us); on a single sequence (8 units of
+// 256 rows, 2048 prefix) MT = 1 wins, 43 against 47 us.
+int choose_mt(const AttnArgs& a) {
+  const int units2 = a.batch * a.hkv * ((a.group * a.n + 2 * kBM - 1) / (2 * kBM));
+  return units2 * 4 <= sm_count() ? 1 : 2;
+}
+
+template <int MT>
+Plan make_plan_mt(const AttnArgs& a) {
+  using C = Cfg<MT>;
   Plan pl{};
+  pl.mt = MT;
   const int R = a.group * a.n;
-  pl.qgroups = (R + kQRows - 1) / kQRows;
+  pl.qgroups = (R + C::kQRows - 1) / C::kQRows;
   pl.pairs = a.batch * a.hkv * pl.qgroups;
   pl.varlen = a.cu_seqlens != nullptr;
   const int sms = sm_count();
@@ -871,20 +958,20 @@ Plan make_plan(const AttnArgs& a) {
     pl.tiles_per_pair = 0;
     pl.grid = a.splits > 0 ? a.splits : sms;
   } else {
-    pl.tiles_per_pair = (a.kv_len + kBN - 1) / kBN;
+    pl.tiles_per_pair = (a.kv_len + C::kBN - 1) / C::kBN;
     const int64_t T = static_cast<int64_t>(pl.pairs) * pl.tiles_per_pair;
     if (a.splits > 0) {
       pl.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(a.splits, T)));
     } else {
-      // Whole pairs per CTA avoid the partial write, the arrival atomics and
-      // the merge, which cost about a fifth of a pair's time on a loaded GPU
-      // (measured on the 16 x 8192-row Llama-3-8B layer); take them unless
-      // stream-K's even split is more than that much shorter.
+      // Whole units per CTA avoid the partial write and the merge, which cost
+      // about a fifth of a unit's time on a loaded GPU (measured on the 16 x
+      // 8192-row Llama-3-8B layer); take them unless stream-K's even split is
+      // more than that much shorter.
       const int64_t per_cta = (pl.pairs + sms - 1) / sms;
       const int64_t cost_pairs = per_cta * pl.tiles_per_pair;
       if (cost_pairs * 5 <= ((T + sms - 1) / sms) * 6) {
         pl.pair_align = true;
-        pl.grid = static_cast<int>((pl.pairs + per_cta - 1) / per_cta);
+        pl.grid = static_cast<int>(std::min<int64_t>(sms, pl.pairs));
       } else {
         // at least 4 tiles per CTA so partials stay a small share of the work
         pl.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, (T + 3) / 4)));
@@ -894,6 +981,8 @@ Plan make_plan(const AttnArgs& a) {
   return pl;
 }
 
+Plan make_plan(const AttnArgs& a) { return choose_mt(a) == 1 ? make_plan_mt<1>(a) : make_plan_mt<2>(a); }
+
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -902,11 +991,12 @@ struct WsLayout {
 };
 
 WsLayout ws_layout(const Plan& pl) {
+  const size_t rows = static_cast<size_t>(pl.mt) * kBM;
   WsLayout w{};
   size_t off = 0;
   w.tile_start = off; off += align_up(static_cast<size_t>(pl.pairs + 1) * sizeof(int));
-  w.part_lse = off;   off += align_up(static_cast<size_t>(pl.grid) * 2 * kQRows * sizeof(float));
-  w.part_o = off;     off += align_up(static_cast<size_t>(pl.grid) * 2 * kQRows * kD * sizeof(float));
+  w.part_lse = off;   off += align_up(static_cast<size_t>(pl.grid) * 2 * rows * sizeof(float));
+  w.part_o = off;     off += align_up(static_cast<size_t>(pl.grid) * 2 * rows * kD * sizeof(float));
   w.total = off;
   return w;
 }
@@ -915,7 +1005,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device)
 // rather than on every launch.
-int ensure_smem_limit(const void* fn) {
+int ensure_smem_limit(const void* fn, uint32_t bytes) {
   static std::mutex mu;
   static std::vector<std::pair<const void*, int>> done;
   int dev = 0;
@@ -924,10 +1014,31 @@ int ensure_smem_limit(const void* fn) {
   std::lock_guard<std::mutex> lock(mu);
   for (const auto& e : done)
     if (e.first == fn && e.second == dev) return GORGON_OK;
-  rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+  rc = check_cuda(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
                   "tcgen05 smem attribute");
   if (!rc) done.emplace_back(fn, dev);
   return rc;
+}
+
+template <int MT>
+int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& kmap, const CUtensorMap& vmap,
+              TcArgs& t, cudaStream_t st) {
+  using C = Cfg<MT>;
+  int rc = GORGON_OK;
+  if (pl.varlen) {
+    attn_tc_prologue<MT><<<1, 32, 0, st>>>(t);
+    rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
+    if (rc) return rc;
+  }
+  auto kern = a.n <= 64 ? (dtype == GORGON_BF16 ? attn_tc_kernel<MT, 2, true> : attn_tc_kernel<MT, 2, false>)
+                        : (dtype == GORGON_BF16 ? attn_tc_kernel<MT, 8, true> : attn_tc_kernel<MT, 8, false>);
+  rc = ensure_smem_limit(reinterpret_cast<const void*>(kern), C::kSmemBytes);
+  if (rc) return rc;
+  kern<<<pl.grid, C::kThreads, C::kSmemBytes, st>>>(kmap, vmap, t);
+  rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
+  if (rc || pl.pair_align) return rc;
+  attn_tc_combine<MT><<<dim3(pl.pairs, C::kQRows / kCombineRows), kCombineThreads, 0, st>>>(t);
+  return check_cuda(cudaGetLastError(), "tcgen05 combine launch");
 }
 
 }  // namespace
@@ -959,6 +1070,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(GORGON_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
   const CUtensorMapDataType tdt = dtype == GORGON_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const cuuint32_t bn = pl.mt == 1 ? Cfg<1>::kBN : Cfg<2>::kBN;  // box rows = K/V tile rows
   CUtensorMap kmap, vmap;
   const void* srcs[2] = {a.k, a.v};
   const int64_t ss[2] = {a.k_ss, a.v_ss}, sh[2] = {a.k_sh, a.v_sh}, sb[2] = {a.k_sb, a.v_sb};
@@ -970,7 +1082,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
       const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.hkv),
                                   static_cast<cuuint64_t>(a.kv_rows)};
       const cuuint64_t strides[2] = {static_cast<cuuint64_t>(sh[m]) * 2, static_cast<cuuint64_t>(ss[m]) * 2};
-      const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(kBN)};
+      const cuuint32_t box[3] = {64, 1, bn};
       r = enc(maps[m], tdt, 3, const_cast<void*>(srcs[m]), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
@@ -978,7 +1090,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
                                   static_cast<cuuint64_t>(a.hkv), static_cast<cuuint64_t>(a.batch)};
       const cuuint64_t strides[3] = {static_cast<cuuint64_t>(ss[m]) * 2, static_cast<cuuint64_t>(sh[m]) * 2,
                                      static_cast<cuuint64_t>(sb[m]) * 2};
-      const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(kBN), 1, 1};
+      const cuuint32_t box[4] = {64, bn, 1, 1};
       r = enc(maps[m], tdt, 4, const_cast<void*>(srcs[m]), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
@@ -1001,21 +1113,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.part_o = reinterpret_cast<float*>(ws + w.part_o);
   t.out_vec = a.out_dtype == GORGON_BF16 && aligned16(a.out) && a.o_sb % 8 == 0 && a.o_sh % 8 == 0 &&
               a.o_sn % 8 == 0;
-  int rc = GORGON_OK;
-  if (pl.varlen) {
-    attn_tc_prologue<<<1, 32, 0, st>>>(t);
-    rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
-    if (rc) return rc;
-  }
-  auto kern = a.n <= 64 ? (dtype == GORGON_BF16 ? attn_tc_kernel<2, true> : attn_tc_kernel<2, false>)
-                        : (dtype == GORGON_BF16 ? attn_tc_kernel<8, true> : attn_tc_kernel<8, false>);
-  rc = ensure_smem_limit(reinterpret_cast<const void*>(kern));
-  if (rc) return rc;
-  kern<<<pl.grid, kThreads, kSmemBytes, st>>>(kmap, vmap, t);
-  rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
-  if (rc || pl.pair_align) return rc;
-  attn_tc_combine<<<dim3(pl.pairs, kQRows / kCombineRows), kCombineThreads, 0, st>>>(t);
-  return check_cuda(cudaGetLastError(), "tcgen05 combine launch");
+  return pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, t, st) : launch_mt<2>(a, dtype, pl, kmap, vmap, t, st);
 }
 
 }  // namespace gorgon

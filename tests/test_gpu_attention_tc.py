@@ -133,6 +133,19 @@ def test_tc_wide_best_first_tree():
     np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
 
 
+def test_tc_wide_trees_over_many_units():
+    """256-node best-first trees on enough (sequence, kv head) units that the
+    kernel takes two 128-row M-tiles per CTA (8-word ancestor masks), against
+    the CUDA-core kernel."""
+    B, Hq, Hkv, N, P = 4, 32, 8, 256, 700
+    rng = random.Random(7)
+    pars = torch.tensor([best_first_tree(rng, 4, 4, N)[0] for _ in range(B)], device="cuda")
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, seed=7)
+    a = G.fused_tree_verify(q, k, v, pars, max_depth=8, backend="tcgen05")
+    b = G.fused_tree_verify(q, k, v, pars, max_depth=8, backend="simt")
+    torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
+
+
 def test_auto_picks_tensor_cores_for_64_node_trees():
     q, k, v = _inputs(1, 32, 8, 64, 512)
     par = _trees(1, 64, 0)[0]
