@@ -526,6 +526,16 @@ def cpu_slices(cfg: dict, count: int, seed: int = 0):
         yield q, k, v, O.prefix_tree_mask(par, P, cfg["max_depth"]), P + N
 
 
+def use_all_host_threads() -> None:
+    """Lets numpy's BLAS use every host thread (torchrun sets OMP_NUM_THREADS=1
+    for each rank; the reference arm runs on rank 0 alone)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(os.cpu_count() or 1)
+    except Exception:  # pragma: no cover
+        pass
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -695,6 +705,8 @@ def run_ours(args):
         raise SystemExit("bench.py needs a CUDA device")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    # NCCL's version banner goes to stdout, where rank 0's JSON line must be alone
+    os.environ["NCCL_DEBUG"] = "WARN"
     sharding.init(sharding.dist_env(), "nccl", dev, timeout_s=120)
     G.load_library()
     # weak scaling by sequence: rank r verifies global sequences [r*B, (r+1)*B)
@@ -767,6 +779,7 @@ def run_reference(args):
     world, rank, _ = dist_setup()
     if rank != 0:
         return
+    use_all_host_threads()
     from oracle import gorgon_oracle as O
     cfg = WORKLOADS[args.workload]
     if cfg.get("kind", "attn") != "attn":
