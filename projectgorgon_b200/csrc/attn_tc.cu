@@ -68,6 +68,7 @@ constexpr uint32_t kOffQ = 0;                          // [mtile][half]
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // + (buf * MT + mtile) * BN
 constexpr uint32_t kColO = 256;  // + mtile * 128
+constexpr int kOutBf16 = 1, kOutF16 = 2, kOutF32 = 3;  // TcArgs::out_vec
 
 // The constants that follow from MT, the 128-row M-tiles per CTA.
 template <int MT>
@@ -96,7 +97,7 @@ struct TcArgs {
   int grid;
   int pair_align;     // whole units per CTA, strided by the grid (no partials to merge)
   int ab_fmt;         // 0 f16, 1 bf16
-  int out_vec;        // bf16 output with 16-byte aligned rows
+  int out_vec;        // 16-byte aligned output rows: kOutBf16 / kOutF16 / kOutF32, else 0
   float* part_o;      // [grid * 2][rows per unit][128]
   float* part_lse;    // [grid * 2][rows per unit]
   int* tile_start;    // varlen: [units + 1] tile prefix (written by attn_tc_prologue)
@@ -200,6 +201,40 @@ struct Segments {
 // tile whose rows are 128 bytes.
 __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
   return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+
+// Packed query row -> (query head within the kv group, tree node), advanced
+// two rows at a time (the rows a half-warp visits in the coalesced Q load and
+// output store).
+struct RowCursor {
+  int pr, gq, node;
+  __device__ __forceinline__ RowCursor(int p, int n) : pr(p), gq(p / n), node(p - (p / n) * n) {}
+  __device__ __forceinline__ void next2(int n) {
+    pr += 2;
+    node += 2;
+    while (node >= n) {  // at most twice: n >= 1
+      node -= n;
+      ++gq;
+    }
+  }
+};
+
+// A softmax warp's 32 rows of its M-tile's Q buffer (two 4 KB pieces, one per
+// d half) double as the warp's staging area for output rows: row rr (0..31)
+// holds 16 chunks of 16 bytes in the same SW128 order as Q, so a thread
+// writing its own row and a half-warp reading one row are both free of bank
+// conflicts.
+__device__ __forceinline__ uint8_t* stage_at(uint8_t* q_tile, int wq, int rr, int j) {
+  return q_tile + (j >> 3) * kQHalf + sw128(static_cast<uint32_t>(wq * 32 + rr), static_cast<uint32_t>(j & 7));
+}
+
+__device__ __forceinline__ uint32_t pack16x2(float x, float y, bool bf16) {
+  if (bf16) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<const uint32_t*>(&v);
+  }
+  const __half2 v = __floats2half2_rn(x, y);
+  return *reinterpret_cast<const uint32_t*>(&v);
 }
 
 __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
@@ -443,24 +478,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
-// Writes 32 finished output columns of one row (bf16 fast path or any dtype).
+// Writes 32 finished output columns of one row in any output dtype or layout
+// (the path for rows that are not 16-byte aligned).
 __device__ __forceinline__ void store_cols32(const TcArgs& t, int64_t ob, int col0, const float (&v)[32]) {
-  if (t.out_vec) {
-    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(t.a.out) + ob + col0;
 #pragma unroll
-    for (int c = 0; c < 32; c += 8) {
-      uint32_t w[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const __nv_bfloat162 v2 = __floats2bfloat162_rn(v[c + 2 * u], v[c + 2 * u + 1]);
-        w[u] = *reinterpret_cast<const uint32_t*>(&v2);
-      }
-      *reinterpret_cast<uint4*>(dst + c) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < 32; ++c) store_as(t.a.out, t.a.out_dtype, ob + col0 + c, v[c]);
-  }
+  for (int c = 0; c < 32; ++c) store_as(t.a.out, t.a.out_dtype, ob + col0 + c, v[c]);
 }
 
 template <int MT, int ANCW, bool BF16>
@@ -495,22 +517,32 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     const int P = pi.L - a.n;
     const bool len_ok = pi.L >= a.n;
 
-    // ---- Q row -> shared memory (SW128 K-major), then hand it to the MMA
-    // warp.  Each half of the row (8 chunks) is loaded before any of it is
-    // stored, so the row costs two memory round trips rather than one per
-    // chunk.
+    // ---- Q rows -> shared memory (SW128 K-major), then hand them to the MMA
+    // warp.  Each warp fills its own 32 rows, a half-warp per 256-byte row, so
+    // a load instruction reads two whole rows (a row per thread would touch 32
+    // cache lines per instruction and keep the load unit busy for
+    // microseconds); 8 rows per half-warp are in flight per round trip.
     const bool walk = a.mask_kind == GORGON_MASK_PARENTS;
     {
-      const uint4* src = reinterpret_cast<const uint4*>(
-          static_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(pi.b) * a.q_sb +
-          static_cast<int64_t>(h) * a.q_sh + static_cast<int64_t>(node) * a.q_sn);
+      const int sub = lane >> 4, jc = lane & 15;  // row parity and 16-byte chunk
+      const int prow0 = pi.qg * C::kQRows + wg * kBM + wq * 32 + sub;  // packed row of the first pass
+      const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(pi.b) * a.q_sb +
+                                static_cast<int64_t>(pi.kvh) * a.group * a.q_sh;
+      constexpr int kBatch = 8;  // rows in flight per half-warp
+      RowCursor rc(prow0, a.n);
+#pragma unroll 1
+      for (int hh = 0; hh < 16 / kBatch; ++hh) {
+        uint4 qv[kBatch];
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint4 qv[8];
+        for (int k = 0; k < kBatch; ++k) {
+          const uint4* src = reinterpret_cast<const uint4*>(qb + static_cast<int64_t>(rc.gq) * a.q_sh +
+                                                            static_cast<int64_t>(rc.node) * a.q_sn) + jc;
+          qv[k] = rc.pr < R ? __ldg(src) : make_uint4(0, 0, 0, 0);
+          rc.next2(a.n);
+        }
 #pragma unroll
-        for (int c = 0; c < 8; ++c) qv[c] = row_ok ? __ldg(src + half * 8 + c) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(q_tile + half * kQHalf + sw128(r, c)) = qv[c];
+        for (int k = 0; k < kBatch; ++k)
+          *reinterpret_cast<uint4*>(stage_at(q_tile, wq, sub + 2 * (hh * kBatch + k), jc)) = qv[k];
       }
       fence_proxy_async_smem();
       tc_fence_before();  // the previous segment's O reads precede the next MMAs
@@ -688,9 +720,86 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
                        static_cast<int64_t>(node) * a.o_sn;
     const uint32_t o_addr = lane_base + kColO + wg * kD;
-    const float inv = 1.f / l;  // l == 0: no visible key, NaN like softmax
     const float lse2 = (l > 0.f) ? m_used + __log2f(l) : -INFINITY;
-    if (whole) {
+    // The rows go out through the warp's staging rows (its slice of the Q
+    // tile, free now that the segment's last Q.K^T has completed) so that
+    // every store instruction writes whole rows.  A piece of a unit cut
+    // between CTAs writes fp32 partials (0 where nothing was visible) into
+    // slot 0 when it starts the CTA's range, else slot 1.
+    const int64_t slot = static_cast<int64_t>(cta) * 2 + ((pi.start <= g0) ? 0 : 1);
+    const int sub = lane >> 4, jc = lane & 15;
+    const int prow0 = pi.qg * C::kQRows + wg * kBM + wq * 32 + sub;
+    const int mode = whole ? t.out_vec : kOutF32;
+    const float inv = 1.f / l;  // whole, l == 0: no visible key, NaN like softmax
+    const bool zero = !whole && !(l > 0.f);
+    if (mode == kOutBf16 || mode == kOutF16) {
+#pragma unroll
+      for (int ch = 0; ch < kD / 32; ++ch) {
+        uint32_t ov[32];
+        tmem_ld32(o_addr + ch * 32, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = pack16x2(__uint_as_float(ov[8 * u + 2 * e]) * inv, __uint_as_float(ov[8 * u + 2 * e + 1]) * inv,
+                            mode == kOutBf16);
+          *reinterpret_cast<uint4*>(stage_at(q_tile, wq, lane, ch * 4 + u)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      __syncwarp();
+      uint16_t* ob16 = static_cast<uint16_t*>(a.out) + static_cast<int64_t>(pi.b) * a.o_sb +
+                       static_cast<int64_t>(pi.kvh) * a.group * a.o_sh;
+      RowCursor rc(prow0, a.n);
+#pragma unroll 4
+      for (int k = 0; k < 16; ++k) {
+        const uint4 v = *reinterpret_cast<const uint4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
+        if (rc.pr < R)
+          *reinterpret_cast<uint4*>(ob16 + static_cast<int64_t>(rc.gq) * a.o_sh + static_cast<int64_t>(rc.node) * a.o_sn +
+                                    jc * 8) = v;
+        rc.next2(a.n);
+      }
+      __syncwarp();
+    } else if (mode == kOutF32) {
+      // fp32 rows are 512 bytes: two passes of 64 columns through the staging rows
+#pragma unroll
+      for (int ps = 0; ps < 2; ++ps) {
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t ov[32];
+          tmem_ld32(o_addr + (ps * 2 + c2) * 32, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<float4*>(stage_at(q_tile, wq, lane, c2 * 8 + u)) =
+                zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                     : make_float4(__uint_as_float(ov[4 * u]) * inv, __uint_as_float(ov[4 * u + 1]) * inv,
+                                   __uint_as_float(ov[4 * u + 2]) * inv, __uint_as_float(ov[4 * u + 3]) * inv);
+        }
+        __syncwarp();
+        if (whole) {
+          float* of = static_cast<float*>(a.out) + static_cast<int64_t>(pi.b) * a.o_sb +
+                      static_cast<int64_t>(pi.kvh) * a.group * a.o_sh + ps * 64 + jc * 4;
+          RowCursor rc(prow0, a.n);
+#pragma unroll 4
+          for (int k = 0; k < 16; ++k) {
+            const float4 v = *reinterpret_cast<const float4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
+            if (rc.pr < R)
+              *reinterpret_cast<float4*>(of + static_cast<int64_t>(rc.gq) * a.o_sh +
+                                         static_cast<int64_t>(rc.node) * a.o_sn) = v;
+            rc.next2(a.n);
+          }
+        } else {
+          float* po = t.part_o + (slot * C::kQRows + wg * kBM + wq * 32) * kD + ps * 64 + jc * 4;
+#pragma unroll 4
+          for (int k = 0; k < 16; ++k)
+            *reinterpret_cast<float4*>(po + (sub + 2 * k) * kD) =
+                *reinterpret_cast<const float4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
+        }
+        __syncwarp();
+      }
+    } else {
 #pragma unroll
       for (int ch = 0; ch < kD / 32; ++ch) {
         uint32_t ov[32];
@@ -701,26 +810,12 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
         for (int c = 0; c < 32; ++c) vals[c] = __uint_as_float(ov[c]) * inv;
         if (row_ok) store_cols32(t, ob, ch * 32, vals);
       }
+    }
+    if (whole) {
       if (row_ok && a.lse) a.lse[orow] = lse2 * 0.6931471805599453f;
-      continue;
+    } else {
+      t.part_lse[slot * C::kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
     }
-    // partial: slot 0 when this piece of the unit starts the CTA's range, else slot 1
-    const int which = (pi.start <= g0) ? 0 : 1;
-    const int64_t slot = static_cast<int64_t>(cta) * 2 + which;
-    float* po = t.part_o + (slot * C::kQRows + qrow) * kD;
-    const bool any = l > 0.f;
-#pragma unroll
-    for (int ch = 0; ch < kD / 32; ++ch) {
-      uint32_t ov[32];
-      tmem_ld32(o_addr + ch * 32, ov);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 32; c += 4)
-        *reinterpret_cast<float4*>(po + ch * 32 + c) =
-            make_float4(any ? __uint_as_float(ov[c]) * inv : 0.f, any ? __uint_as_float(ov[c + 1]) * inv : 0.f,
-                        any ? __uint_as_float(ov[c + 2]) * inv : 0.f, any ? __uint_as_float(ov[c + 3]) * inv : 0.f);
-    }
-    t.part_lse[slot * C::kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
   }
 }
 
@@ -821,13 +916,18 @@ __global__ void attn_tc_prologue(const TcArgs t) {
 // Merges the pieces of every unit that the stream-K schedule cut between
 // CTAs: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M) with M = max_k
 // lse_k (log2 units) and o_k each piece's normalised output.  Grid (units,
-// rows per unit / kCombineRows): a warp takes one row, a lane one piece's lse
-// (32 pieces at a time) and four of the row's columns, so a row costs two
-// memory round trips (the lse values, then every piece's 512-byte row,
-// coalesced, 8 pieces in flight per lane).  Units that one CTA finished are
-// skipped.
-constexpr int kCombineRows = 8;  // rows per CTA: one per warp
-constexpr int kCombineThreads = 256;
+// rows per unit / 32), 8 warps of 4 rows each.  One thread works out the
+// unit's pieces (their CTAs and workspace slots) for the block.  With at most
+// kCombineFast pieces (every unit of a batch large enough to fill the GPU) a
+// warp issues the lse values of its 4 rows in one round trip (8 lanes per
+// row) and then every piece's 512-byte row of all 4 rows in another, a lane
+// holding four columns; more pieces go row by row, 32 lse values and 8
+// pieces' rows in flight at a time.  Units that one CTA finished are skipped.
+constexpr int kCombineWarps = 8;
+constexpr int kCombineThreads = kCombineWarps * 32;
+constexpr int kCombineRowsPerWarp = 4;
+constexpr int kCombineRows = kCombineWarps * kCombineRowsPerWarp;  // rows per CTA
+constexpr int kCombineFast = 4;                                    // pieces per row on the fast path
 
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
@@ -835,77 +935,146 @@ __device__ __forceinline__ float warp_max(float x) {
   return x;
 }
 
+// Writes four consecutive output columns of one row.
+__device__ __forceinline__ void store4(const TcArgs& t, int64_t idx, float x, float y, float z, float w) {
+  if (t.out_vec == kOutBf16 || t.out_vec == kOutF16) {
+    const bool bf = t.out_vec == kOutBf16;
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(t.a.out) + idx) = make_uint2(pack16x2(x, y, bf), pack16x2(z, w, bf));
+  } else if (t.out_vec == kOutF32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(t.a.out) + idx) = make_float4(x, y, z, w);
+  } else {
+    store_as(t.a.out, t.a.out_dtype, idx, x);
+    store_as(t.a.out, t.a.out_dtype, idx + 1, y);
+    store_as(t.a.out, t.a.out_dtype, idx + 2, z);
+    store_as(t.a.out, t.a.out_dtype, idx + 3, w);
+  }
+}
+
 template <int MT>
 __global__ void __launch_bounds__(kCombineThreads) attn_tc_combine(const TcArgs t) {
   constexpr int kQRows = Cfg<MT>::kQRows;
+  __shared__ long long s_slot0, s_first;
+  __shared__ int s_parts;
   const PairInfo pi = pair_info(t, blockIdx.x);
-  if (pi.end <= pi.start) return;
-  const int64_t T = total_tiles(t);
-  const int64_t first = cta_of(pi.start, T, t.grid);
-  const int64_t last = cta_of(pi.end - 1, T, t.grid);
-  if (first == last) return;
-  const int parts = static_cast<int>(last - first + 1);
-  // a piece's slot: 1 when it is the second unit of its CTA's range
-  auto slot = [&](int64_t c) -> int64_t {
-    return c * 2 + ((c == first && pi.start > range_start(c, T, t.grid)) ? 1 : 0);
-  };
+  if (threadIdx.x == 0) {
+    int parts = 0;
+    if (pi.end > pi.start) {
+      const int64_t T = total_tiles(t);
+      const int64_t first = cta_of(pi.start, T, t.grid);
+      parts = static_cast<int>(cta_of(pi.end - 1, T, t.grid) - first + 1);
+      s_first = first;
+      // slot 1 when the unit is the second one in its first CTA's range
+      s_slot0 = first * 2 + (pi.start > range_start(first, T, t.grid) ? 1 : 0);
+    }
+    s_parts = parts;
+  }
+  __syncthreads();
+  const int parts = s_parts;
+  if (parts <= 1) return;
+  const int64_t first = s_first, slot0 = s_slot0;
+  auto slot = [&](int j) -> int64_t { return j == 0 ? slot0 : (first + j) * 2; };
   const AttnArgs& a = t.a;
   const int R = a.group * a.n;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qrow = blockIdx.y * kCombineRows + warp;
-  const int pr = pi.qg * kQRows + qrow;
-  if (pr >= R) return;
-  const int gq = pr / a.n, node = pr % a.n;
-  const int h = pi.kvh * a.group + gq;
-  const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
-  const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
-                     static_cast<int64_t>(node) * a.o_sn;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float M = -INFINITY, wsum = 0.f;
-  for (int c0 = 0; c0 < parts; c0 += 32) {
-    // lane j holds piece c0 + j's lse; the group's max rescales what came before
-    const int cj = c0 + lane;
-    const float lj = cj < parts ? __ldcg(t.part_lse + slot(first + cj) * kQRows + qrow) : -INFINITY;
-    const float Mn = fmaxf(M, warp_max(lj));
-    if (Mn == -INFINITY) continue;  // nothing visible yet
-    const float r = ex2_approx(M - Mn);  // 0 while M was -inf
-    acc.x *= r; acc.y *= r; acc.z *= r; acc.w *= r;
-    wsum *= r;
-    M = Mn;
-    const float wj = ex2_approx(lj - M);  // 0 for pieces past the end or with nothing visible
-    const int n_here = min(32, parts - c0);
-    for (int j0 = 0; j0 < n_here; j0 += 8) {
-      float4 v[8];
+  const int qrow0 = blockIdx.y * kCombineRows + warp * kCombineRowsPerWarp;
+  const int pr0 = pi.qg * kQRows + qrow0;  // packed row of the warp's first row
+  // Finishes row k from its weighted sum: NaN (and lse -inf) when no piece saw a key.
+  auto finish = [&](int k, float M, float wsum, float4 acc) {
+    const int pr = pr0 + k;
+    const int gq = pr / a.n, node = pr - gq * a.n;
+    const int h = pi.kvh * a.group + gq;
+    const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
+    const int64_t ob =
+        static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh + static_cast<int64_t>(node) * a.o_sn;
+    if (M == -INFINITY) {
+      store4(t, ob + lane * 4, NAN, NAN, NAN, NAN);
+      if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
+      return;
+    }
+    const float winv = 1.f / wsum;
+    store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv);
+    if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+  };
+
+  if (parts <= kCombineFast) {
+    // lanes 8k .. 8k + 7 hold row k's piece lse values
+    const int kr = lane >> 3, jp = lane & 7;
+    float lj = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        v[j] = j0 + j < n_here
-                   ? __ldcg(reinterpret_cast<const float4*>(t.part_o + (slot(first + c0 + j0 + j) * kQRows + qrow) *
-                                                                           kD) + lane)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < kCombineRowsPerWarp; ++k)
+      if (k == kr && pr0 + k < R && jp < parts) lj = __ldcg(t.part_lse + slot(jp) * kQRows + qrow0 + k);
+    float4 v[kCombineRowsPerWarp][kCombineFast];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float w = __shfl_sync(0xffffffffu, wj, (j0 + j) & 31);
-        if (j0 + j < n_here) {
-          wsum += w;
-          acc.x = fmaf(w, v[j].x, acc.x);
-          acc.y = fmaf(w, v[j].y, acc.y);
-          acc.z = fmaf(w, v[j].z, acc.z);
-          acc.w = fmaf(w, v[j].w, acc.w);
+    for (int k = 0; k < kCombineRowsPerWarp; ++k)
+#pragma unroll
+      for (int j = 0; j < kCombineFast; ++j)
+        v[k][j] = (pr0 + k < R && j < parts)
+                      ? __ldcg(reinterpret_cast<const float4*>(t.part_o + (slot(j) * kQRows + qrow0 + k) * kD) + lane)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = lj;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float wj = M == -INFINITY ? 0.f : ex2_approx(lj - M);  // 0 for missing pieces
+#pragma unroll
+    for (int k = 0; k < kCombineRowsPerWarp; ++k) {
+      const float Mk = __shfl_sync(0xffffffffu, M, 8 * k);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float wsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < kCombineFast; ++j) {
+        const float w = __shfl_sync(0xffffffffu, wj, 8 * k + j);
+        wsum += w;
+        acc.x = fmaf(w, v[k][j].x, acc.x);
+        acc.y = fmaf(w, v[k][j].y, acc.y);
+        acc.z = fmaf(w, v[k][j].z, acc.z);
+        acc.w = fmaf(w, v[k][j].w, acc.w);
+      }
+      if (pr0 + k < R) finish(k, Mk, wsum, acc);
+    }
+    return;
+  }
+
+#pragma unroll 1
+  for (int k = 0; k < kCombineRowsPerWarp; ++k) {
+    if (pr0 + k >= R) continue;
+    const int qrow = qrow0 + k;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = -INFINITY, wsum = 0.f;
+    for (int c0 = 0; c0 < parts; c0 += 32) {
+      // lane j holds piece c0 + j's lse; the group's max rescales what came before
+      const int cj = c0 + lane;
+      const float lj = cj < parts ? __ldcg(t.part_lse + slot(cj) * kQRows + qrow) : -INFINITY;
+      const float Mn = fmaxf(M, warp_max(lj));
+      if (Mn == -INFINITY) continue;  // nothing visible yet
+      const float r = ex2_approx(M - Mn);  // 0 while M was -inf
+      acc.x *= r; acc.y *= r; acc.z *= r; acc.w *= r;
+      wsum *= r;
+      M = Mn;
+      const float wj = ex2_approx(lj - M);  // 0 for pieces past the end or with nothing visible
+      const int n_here = min(32, parts - c0);
+      for (int j0 = 0; j0 < n_here; j0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = j0 + j < n_here
+                     ? __ldcg(reinterpret_cast<const float4*>(t.part_o + (slot(c0 + j0 + j) * kQRows + qrow) * kD) +
+                              lane)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float w = __shfl_sync(0xffffffffu, wj, (j0 + j) & 31);
+          if (j0 + j < n_here) {
+            wsum += w;
+            acc.x = fmaf(w, v[j].x, acc.x);
+            acc.y = fmaf(w, v[j].y, acc.y);
+            acc.z = fmaf(w, v[j].z, acc.z);
+            acc.w = fmaf(w, v[j].w, acc.w);
+          }
         }
       }
     }
+    finish(k, M, wsum, acc);
   }
-  if (M == -INFINITY) {  // no visible key in any piece: NaN, like softmax
-    for (int c = lane; c < kD; c += 32) store_as(a.out, a.out_dtype, ob + c, NAN);
-    if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
-    return;
-  }
-  const float winv = 1.f / wsum;
-  store_as(a.out, a.out_dtype, ob + lane * 4, acc.x * winv);
-  store_as(a.out, a.out_dtype, ob + lane * 4 + 1, acc.y * winv);
-  store_as(a.out, a.out_dtype, ob + lane * 4 + 2, acc.z * winv);
-  store_as(a.out, a.out_dtype, ob + lane * 4 + 3, acc.w * winv);
-  if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
 }
 
 // ------------------------------------------------------------ host side
@@ -1111,8 +1280,14 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.tile_start = reinterpret_cast<int*>(ws + w.tile_start);
   t.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   t.part_o = reinterpret_cast<float*>(ws + w.part_o);
-  t.out_vec = a.out_dtype == GORGON_BF16 && aligned16(a.out) && a.o_sb % 8 == 0 && a.o_sh % 8 == 0 &&
-              a.o_sn % 8 == 0;
+  {
+    // rows of whole 16-byte chunks: strides in elements that are multiples of 16 bytes
+    const int per16 = a.out_dtype == GORGON_F32 ? 4 : 8;
+    const bool rows16 = aligned16(a.out) && a.o_sb % per16 == 0 && a.o_sh % per16 == 0 && a.o_sn % per16 == 0;
+    t.out_vec = !rows16 ? 0
+                        : a.out_dtype == GORGON_BF16 ? kOutBf16
+                                                     : (a.out_dtype == GORGON_F16 ? kOutF16 : kOutF32);
+  }
   return pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, t, st) : launch_mt<2>(a, dtype, pl, kmap, vmap, t, st);
 }
 
