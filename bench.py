@@ -191,7 +191,8 @@ class Workload:
     def e2e(self, steps: int, warmup: int, world: int):
         ms, h2d, d2h = time_e2e(self, steps, warmup, world)
         return ms, h2d, d2h, ("prefix K/V cache resident in HBM; per step the tree's Q, K/V rows and "
-                              "parents are copied in and the output copied out")
+                              "parents are copied in and the output copied out, pipelined: step i + 1's "
+                              "copy-in and step i - 1's copy-out overlap step i's compute")
 
     def cpu_baseline(self, budget_s: float):
         return cpu_baseline(self, budget_s=budget_s)
@@ -615,7 +616,12 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
 def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     """Each step: H2D of Q, the tree's K/V rows and parents from pinned host
     memory, the tree rows written into the resident cache, the attention
-    call, and D2H of the output."""
+    call, and D2H of the output.  Steps are pipelined the way a serving loop
+    overlaps transfers with compute: step i + 1's inputs are copied in on one
+    stream while step i computes on another, and step i's output is copied out
+    on a third; two sets of device input buffers alternate.  The timed region
+    starts before the first step's copy-in and ends after the last step's
+    copy-out, so every step's transfers lie inside it."""
     dev = wl.dev
     cfg = wl.cfg
     B, N = cfg["B"], cfg["N"]
@@ -629,41 +635,62 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
         P = wl.prefixes[0]
         kt_h = wl.k[:, :, P:P + N].contiguous().cpu().pin_memory()
         vt_h = wl.v[:, :, P:P + N].contiguous().cpu().pin_memory()
-    out_h = torch.empty(wl.q.shape, dtype=wl.q.dtype).pin_memory()
-    q_d = torch.empty_like(wl.q)
-    kt_d = torch.empty(kt_h.shape, dtype=kt_h.dtype, device=dev)
-    vt_d = torch.empty(vt_h.shape, dtype=vt_h.dtype, device=dev)
-    par_d = torch.empty_like(wl.par_t)
+    nbuf = 2
+    bufs = [(torch.empty_like(wl.q), torch.empty(kt_h.shape, dtype=kt_h.dtype, device=dev),
+             torch.empty(vt_h.shape, dtype=vt_h.dtype, device=dev), torch.empty_like(wl.par_t))
+            for _ in range(nbuf)]
+    outs_h = [torch.empty(wl.q.shape, dtype=wl.q.dtype).pin_memory() for _ in range(nbuf)]
     h2d = sum(t.numel() * t.element_size() for t in (q_h, kt_h, vt_h, par_h))
-    d2h = out_h.numel() * out_h.element_size()
+    d2h = outs_h[0].numel() * outs_h[0].element_size()
+    s_c = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    in_free = [torch.cuda.Event() for _ in range(nbuf)]
+    done = [torch.cuda.Event() for _ in range(nbuf)]
+    kw = wl.kwargs()
 
-    def one():
-        q_d.copy_(q_h, non_blocking=True)
-        kt_d.copy_(kt_h, non_blocking=True)
-        vt_d.copy_(vt_h, non_blocking=True)
-        par_d.copy_(par_h, non_blocking=True)
+    def one(i):
+        k = i % nbuf
+        q_d, kt_d, vt_d, par_d = bufs[k]
+        with torch.cuda.stream(s_in):
+            if i >= nbuf:
+                s_in.wait_event(in_free[k])  # step i - 2 has read this buffer set
+            q_d.copy_(q_h, non_blocking=True)
+            kt_d.copy_(kt_h, non_blocking=True)
+            vt_d.copy_(vt_h, non_blocking=True)
+            par_d.copy_(par_h, non_blocking=True)
+            in_ready[k].record(s_in)
+        s_c.wait_event(in_ready[k])
         if wl.ragged:
             wl.k[rows] = kt_d
             wl.v[rows] = vt_d
         else:
             wl.k[:, :, P:P + N].copy_(kt_d)
             wl.v[:, :, P:P + N].copy_(vt_d)
-        kw = wl.kwargs()
-        kw["parents"] = par_d
-        o = G.fused_tree_verify(q_d, wl.k, wl.v, **kw)
-        out_h.copy_(o, non_blocking=True)
+        o = G.fused_tree_verify(q_d, wl.k, wl.v, **dict(kw, parents=par_d))
+        in_free[k].record(s_c)
+        done[k].record(s_c)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(done[k])
+            outs_h[k].copy_(o, non_blocking=True)
+            o.record_stream(s_out)
 
-    for _ in range(warmup):
-        one()
+    def run(n):
+        for i in range(n):
+            one(i)
+        s_c.wait_stream(s_in)
+        s_c.wait_stream(s_out)
+
+    run(warmup)
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
-    st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(steps):
-        one()
-    e1.record(st)
+    e0.record(s_c)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
+    run(steps)
+    e1.record(s_c)
     torch.cuda.synchronize(dev)
     return e0.elapsed_time(e1), h2d, d2h
 
