@@ -37,6 +37,8 @@ __all__ = [
     "verify_tree",
     "apply_cache_slice",
     "kv_trim",
+    "head_topk",
+    "build_candidate_tree",
 ]
 
 
@@ -305,3 +307,104 @@ def kv_trim(layers: List[Tuple[np.ndarray, np.ndarray]], idx: np.ndarray,
             nv[b, :, d0:d0 + L] = vc[b][:, ii]
         out.append((nk, nv))
     return out
+
+
+def head_topk(logits: np.ndarray, k: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray, float]:
+    """What one Medusa head contributes to a candidate tree
+    (``src/gorgon/inference/tree_candidates.py:42-81``, ``_topk_per_head``):
+    the ``min(k, V)`` largest logits and their ids in descending order (equal
+    logits by ascending id), the softmax over those logits, and the entropy of
+    the softmax over the whole vocabulary, ``-sum p log(p + 1e-10)``.  Computed
+    in float64 from the given logits (the reference works in the logits'
+    dtype)."""
+    x = np.asarray(logits, dtype=np.float64).ravel()
+    kk = min(int(k), x.size)
+    order = np.lexsort((np.arange(x.size), -x))[:kk]
+    scores = x[order]
+    e = np.exp(scores - scores[0])
+    probs = e / e.sum()
+    p = np.exp(x - x.max())
+    p /= p.sum()
+    entropy = float(-(p * np.log(p + 1e-10)).sum())
+    return order.astype(np.int64), scores, probs, entropy
+
+
+def build_candidate_tree(levels, top_k: int, max_candidates: Optional[int] = None,
+                         confidence_threshold: float = 0.0, use_path_confidence: bool = False,
+                         entropy_weighted: bool = False) -> Tuple[List[int], List[int], List[float]]:
+    """Tree assembly of ``build_candidate_tree``
+    (``src/gorgon/inference/tree_candidates.py:92-245``) from the per-head
+    statistics ``levels = [(ids, scores, probs, entropy), ...]`` of
+    :func:`head_topk`, one entry per tree level.  Returns the nodes' tokens,
+    parents (-1 for a root) and probabilities in node order.
+
+    * Level 1 (``:149-172``): head 0's candidates in top-k order become roots,
+      skipping those whose probability is below the level's threshold, until
+      the budget ``max_candidates`` (``None`` = unlimited) is spent.
+    * Later levels (``:175-226``): every node of the previous level, in order
+      of its own logit (descending, stable) when a budget is set and in node
+      order otherwise, gets one child per candidate of the level's head, in
+      top-k order; a child is skipped when its probability is below the
+      threshold or, with ``use_path_confidence``, when the product of
+      probabilities along its path is; nodes are added until the budget is
+      spent.
+    * The threshold is ``confidence_threshold``, scaled by
+      ``1 - entropy / log(top_k)`` (``1 - entropy`` for ``top_k <= 1``) per head
+      when ``entropy_weighted`` (``:151-156``, ``:182-187``).
+    """
+    def threshold(entropy: float) -> float:
+        if confidence_threshold > 0 and entropy_weighted:
+            max_ent = math.log(top_k) if top_k > 1 else 1.0
+            return confidence_threshold * (1.0 - (entropy / max_ent if max_ent > 0 else 0.0))
+        return confidence_threshold
+
+    tokens: List[int] = []
+    parents: List[int] = []
+    probs: List[float] = []
+    path: List[float] = []
+    budget = max_candidates
+    if not levels:
+        return tokens, parents, probs
+    ids0, scores0, probs0, ent0 = levels[0]
+    thr = threshold(ent0)
+    level_nodes: List[Tuple[int, float]] = []
+    for i in range(len(ids0)):
+        if budget is not None and budget <= 0:
+            break
+        pr = float(probs0[i])
+        if confidence_threshold > 0 and pr < thr:
+            continue
+        level_nodes.append((len(tokens), float(scores0[i])))
+        tokens.append(int(ids0[i]))
+        parents.append(-1)
+        probs.append(pr)
+        path.append(pr)
+        if budget is not None:
+            budget -= 1
+    for lv in range(1, len(levels)):
+        if budget is not None and budget <= 0:
+            break
+        ids_l, scores_l, probs_l, ent_l = levels[lv]
+        thr = threshold(ent_l)
+        order = (sorted(level_nodes, key=lambda x: x[1], reverse=True)
+                 if max_candidates is not None else list(level_nodes))
+        nxt: List[Tuple[int, float]] = []
+        for pidx, _ in order:
+            for i in range(len(ids_l)):
+                if budget is not None and budget <= 0:
+                    break
+                pr = float(probs_l[i])
+                if confidence_threshold > 0 and pr < thr:
+                    continue
+                cp = path[pidx] * pr
+                if use_path_confidence and confidence_threshold > 0 and cp < thr:
+                    continue
+                nxt.append((len(tokens), float(scores_l[i])))
+                tokens.append(int(ids_l[i]))
+                parents.append(pidx)
+                probs.append(pr)
+                path.append(cp)
+                if budget is not None:
+                    budget -= 1
+        level_nodes = nxt
+    return tokens, parents, probs

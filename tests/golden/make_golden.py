@@ -20,6 +20,9 @@ Reference functions exercised (file:line within the reference project):
   tests/test_benchmark_inference.py:16-72)
 * ``get_tree_paths``           src/gorgon/inference/tree_candidates.py:282-311
 * ``apply_cache_slice``        src/gorgon/inference/kv_cache.py:89-108
+* ``build_candidate_tree``     src/gorgon/inference/tree_candidates.py:92-245
+  and ``_topk_per_head`` (:42-81), driven by fake Medusa heads that return
+  fixed logits
 """
 from __future__ import annotations
 
@@ -46,7 +49,9 @@ def _load_reference(root: Path):
     from gorgon.inference.tree_candidates import (
         CandidateTree, candidate_tree_to_mask, get_tree_paths)
     from gorgon.inference.kv_cache import apply_cache_slice
+    from gorgon.inference.tree_candidates import build_candidate_tree, _topk_per_head
     return dict(build_tree_mask=build_tree_mask, tree_attention_ref=tree_attention_ref,
+                build_candidate_tree=build_candidate_tree, topk_per_head=_topk_per_head,
                 accept_draft_tokens=accept_draft_tokens,
                 verify=_verify_tree_candidates, CandidateTree=CandidateTree,
                 candidate_tree_to_mask=candidate_tree_to_mask,
@@ -239,13 +244,70 @@ def gen_kv(ref) -> dict:
     return out
 
 
+# name, heads, vocab, top_k, max_depth, max_candidates, threshold, path_conf, entropy_w, sigma
+CAND_CASES = [
+    ("k4_d3", 3, 64, 4, None, None, 0.0, False, False, 2.0),
+    ("k4_d4_budget20", 4, 64, 4, None, 20, 0.0, False, False, 2.0),
+    ("k4_d4_budget64", 4, 200, 4, None, 64, 0.0, False, False, 2.0),
+    ("k3_threshold", 3, 100, 3, None, None, 0.3, False, False, 1.0),
+    ("k5_threshold_entropy", 4, 100, 5, None, None, 0.4, False, True, 5.0),
+    ("k4_threshold_path", 4, 100, 4, None, None, 0.05, True, False, 2.0),
+    ("k4_all_rules", 4, 150, 4, None, 30, 0.1, True, True, 2.5),
+    ("k1_d5", 5, 40, 1, None, None, 0.0, False, False, 1.0),
+    ("k8_d2", 2, 300, 8, None, None, 0.0, False, False, 3.0),
+    ("max_depth2_of4", 4, 64, 4, 2, None, 0.0, False, False, 2.0),
+    ("all_pruned", 3, 64, 4, None, None, 0.99, False, False, 0.1),
+    ("budget0", 3, 64, 4, None, 0, 0.0, False, False, 2.0),
+    ("k_above_vocab", 2, 3, 4, None, None, 0.0, False, False, 1.0),
+    ("k4_d3_budget7_threshold", 3, 80, 4, None, 7, 0.2, False, False, 1.2),
+]
+
+
+class _FixedHead(torch.nn.Module):
+    """A Medusa head stand-in that returns fixed logits (1, 1, vocab)."""
+
+    def __init__(self, logits):
+        super().__init__()
+        self.register_buffer("logits", logits)
+
+    def forward(self, hidden):
+        return self.logits[None, None]
+
+
+def gen_candidates(ref) -> dict:
+    out = {"names": np.array([c[0] for c in CAND_CASES])}
+    g = torch.Generator().manual_seed(11)
+    hidden = torch.zeros(1, 1, 8)
+    for name, nh, vocab, k, md, mc, thr, pc, ew, sigma in CAND_CASES:
+        logits = torch.randn(nh, vocab, generator=g) * sigma
+        heads = torch.nn.ModuleList([_FixedHead(logits[h]) for h in range(nh)])
+        tree = ref["build_candidate_tree"](heads, hidden, top_k=k, max_depth=md, max_candidates=mc,
+                                           confidence_threshold=thr, use_path_confidence=pc,
+                                           entropy_weighted=ew)
+        depth = min(md or nh, nh)
+        stats = ref["topk_per_head"](heads[:depth], hidden, k)
+        out[f"{name}_logits"] = logits.numpy()
+        out[f"{name}_params"] = np.array([k, -1 if md is None else md, -1 if mc is None else mc,
+                                          int(pc), int(ew)], dtype=np.int64)
+        out[f"{name}_threshold"] = np.array(thr, dtype=np.float64)
+        out[f"{name}_tokens"] = tree.tokens.numpy().astype(np.int64)
+        out[f"{name}_parents"] = np.asarray(tree.parents, dtype=np.int64)
+        out[f"{name}_depth"] = np.array(tree.depth)
+        out[f"{name}_scores"] = tree.scores.numpy().astype(np.float32)
+        out[f"{name}_topk_ids"] = np.stack([s.ids.numpy() for s in stats]).astype(np.int64)
+        out[f"{name}_topk_scores"] = np.stack([s.scores.numpy() for s in stats]).astype(np.float32)
+        out[f"{name}_topk_probs"] = np.stack([s.probs.numpy() for s in stats]).astype(np.float32)
+        out[f"{name}_entropy"] = np.array([s.entropy for s in stats], dtype=np.float64)
+    return out
+
+
 def main() -> None:
     root = Path(sys.argv[1]) if len(sys.argv) > 1 else None
     if root is None or not (root / "src" / "gorgon").is_dir():
         raise SystemExit("usage: make_golden.py <ProjectGorgon checkout>")
     ref = _load_reference(root)
     for name, fn in (("tree_mask", gen_masks), ("attention", gen_attention),
-                     ("verify", gen_verify), ("kv_cache", gen_kv)):
+                     ("verify", gen_verify), ("kv_cache", gen_kv), ("candidates", gen_candidates)):
         data = fn(ref)
         np.savez_compressed(HERE / f"{name}.npz", **data)
         print(name, len(data), "arrays")

@@ -102,3 +102,52 @@ def test_kv_trim_equals_apply_cache_slice_per_slice():
                 np.testing.assert_array_equal(nk[b, h, dst[b]:], ek)
                 np.testing.assert_array_equal(nv[b, h, dst[b]:], ev)
                 np.testing.assert_array_equal(nk[b, h, :dst[b]], k[b, h, :dst[b]])
+
+
+CAND = load_golden("candidates")
+
+
+def _cand_case(name):
+    k, md, mc, pc, ew = (int(x) for x in CAND[f"{name}_params"])
+    return dict(top_k=k, max_depth=None if md < 0 else md, max_candidates=None if mc < 0 else mc,
+                confidence_threshold=float(CAND[f"{name}_threshold"]), use_path_confidence=bool(pc),
+                entropy_weighted=bool(ew))
+
+
+@pytest.mark.parametrize("name", list(CAND["names"]))
+def test_head_topk_matches_reference(name):
+    c = _cand_case(name)
+    logits = CAND[f"{name}_logits"]
+    depth = int(CAND[f"{name}_depth"])
+    for h in range(depth):
+        ids, scores, probs, ent = O.head_topk(logits[h], c["top_k"])
+        np.testing.assert_array_equal(ids, CAND[f"{name}_topk_ids"][h])
+        np.testing.assert_allclose(scores, CAND[f"{name}_topk_scores"][h], rtol=0, atol=0)
+        np.testing.assert_allclose(probs, CAND[f"{name}_topk_probs"][h], rtol=1e-6, atol=1e-7)
+        np.testing.assert_allclose(ent, CAND[f"{name}_entropy"][h], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", list(CAND["names"]))
+def test_candidate_tree_matches_reference(name):
+    c = _cand_case(name)
+    logits = CAND[f"{name}_logits"]
+    depth = int(CAND[f"{name}_depth"])
+    levels = [O.head_topk(logits[h], c["top_k"]) for h in range(depth)]
+    toks, pars, probs = O.build_candidate_tree(
+        levels, c["top_k"], max_candidates=c["max_candidates"],
+        confidence_threshold=c["confidence_threshold"], use_path_confidence=c["use_path_confidence"],
+        entropy_weighted=c["entropy_weighted"])
+    np.testing.assert_array_equal(np.asarray(toks, dtype=np.int64), CAND[f"{name}_tokens"])
+    np.testing.assert_array_equal(np.asarray(pars, dtype=np.int64), CAND[f"{name}_parents"])
+    np.testing.assert_allclose(np.asarray(probs, dtype=np.float32), CAND[f"{name}_scores"], rtol=1e-6, atol=1e-7)
+
+
+def test_golden_candidate_cases_cover_every_rule():
+    sizes = {str(n): len(CAND[f"{n}_tokens"]) for n in CAND["names"]}
+    assert sizes["all_pruned"] == 0 and sizes["budget0"] == 0
+    assert sizes["k4_d4_budget20"] == 20 and sizes["k4_d4_budget64"] == 64
+    assert sizes["k4_d3"] == 4 + 16 + 64
+    # thresholds prune something but not everything
+    for n in ("k3_threshold", "k5_threshold_entropy", "k4_threshold_path", "k4_all_rules"):
+        full = sum(int(CAND[f"{n}_params"][0]) ** (l + 1) for l in range(int(CAND[f"{n}_depth"])))
+        assert 0 < sizes[n] < full, n
