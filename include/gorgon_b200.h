@@ -66,8 +66,9 @@ GORGON_API const char* gorgon_last_error(void);
 
 /* Reads (synchronously) the device-side error word of the current device:
  * bit 0 = a parents[] entry outside [-1, n) was met, bit 1 = a KV-trim index
- * outside the cache, bit 2 = a verifier tree/draft entry out of range.  The
- * offending element is skipped, never dereferenced.  clear != 0 resets it. */
+ * outside the cache, bit 2 = a verifier tree/draft entry out of range, bit 3 =
+ * a candidate tree was cut at max_nodes.  The offending element is skipped,
+ * never dereferenced.  clear != 0 resets it. */
 GORGON_API int gorgon_device_error(uint32_t* out_flags, int clear);
 
 /* ------------------------------------------------------------------------
@@ -231,6 +232,60 @@ typedef struct {
 } gorgon_kv_trim_params;
 
 GORGON_API int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Candidate-tree builder.  Replaces build_candidate_tree
+ * (src/gorgon/inference/tree_candidates.py:92-245) with its per-head
+ * statistics _topk_per_head (:42-81), once the Medusa heads have produced
+ * their logits: logits[b, l, :] is the vocabulary row of head l (tree level
+ * l + 1) for sequence b.
+ *
+ * Per row: the min(top_k, vocab) largest logits (descending; equal logits by
+ * ascending id), the softmax over them, and the entropy of the softmax over
+ * the whole row.  Per sequence, the reference's expansion: head 0's
+ * candidates become roots; each later level gives every node of the level
+ * above (in order of that node's own logit, descending and stable, when
+ * max_candidates >= 0; in node order otherwise) one child per candidate of
+ * the level's head, in top-k order.  A candidate is skipped when its
+ * probability -- or, with use_path_confidence, the product of probabilities
+ * along its path -- is below the level's threshold: confidence_threshold
+ * (0 = off), times 1 - entropy / ln(top_k) when entropy_weighted.  Nodes are
+ * added until max_candidates exist (< 0: no budget).
+ *
+ * logits [batch, levels, vocab] (vocab contiguous; finite values).  Outputs,
+ * in node order: tokens int64 [batch, max_nodes], parents int32 [batch,
+ * max_nodes] (-1 = root), probs float [batch, max_nodes], n_nodes int32
+ * [batch]; slots from n_nodes[b] on hold -1 / -1 / 0.  A tree that would
+ * outgrow max_nodes is cut there and sets device error bit 3.  topk_ids
+ * int32, topk_scores and topk_probs float [batch, levels, top_k] and entropy
+ * float [batch, levels] receive the per-row statistics when all four are
+ * non-NULL (the workspace holds them otherwise).  The entropy is
+ * ln Z - sum(e^x (x - max)) / Z, the reference's -sum p log(p + 1e-10)
+ * without the 1e-10 (at most ~1e-5 apart for a 128k vocabulary).
+ * top_k <= 32, max_nodes <= 4096.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  int32_t dtype;  /* gorgon_dtype of logits */
+  const void* logits; int64_t logits_stride_b, logits_stride_l;
+  int64_t batch, levels, vocab;
+  int32_t top_k;
+  int32_t max_candidates;
+  float confidence_threshold;
+  int32_t use_path_confidence, entropy_weighted;
+  int64_t max_nodes;
+  int64_t* tokens;
+  int32_t* parents;
+  float* probs;
+  int32_t* n_nodes;
+  int32_t* topk_ids;
+  float* topk_scores;
+  float* topk_probs;
+  float* entropy;
+} gorgon_candidate_tree_params;
+
+GORGON_API size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tree_params* p);
+GORGON_API int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace,
+                                     size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

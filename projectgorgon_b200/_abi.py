@@ -79,6 +79,21 @@ class KvTrimParams(Structure):
     ]
 
 
+class CandidateTreeParams(Structure):
+    _fields_ = [
+        ("dtype", c_int32),
+        ("logits", c_void_p), ("logits_stride_b", c_int64), ("logits_stride_l", c_int64),
+        ("batch", c_int64), ("levels", c_int64), ("vocab", c_int64),
+        ("top_k", c_int32),
+        ("max_candidates", c_int32),
+        ("confidence_threshold", c_float),
+        ("use_path_confidence", c_int32), ("entropy_weighted", c_int32),
+        ("max_nodes", c_int64),
+        ("tokens", c_void_p), ("parents", c_void_p), ("probs", c_void_p), ("n_nodes", c_void_p),
+        ("topk_ids", c_void_p), ("topk_scores", c_void_p), ("topk_probs", c_void_p), ("entropy", c_void_p),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "gorgon_abi_version": (c_int, []),
@@ -93,6 +108,8 @@ SIGNATURES = {
     "gorgon_verify": (c_int, [POINTER(VerifyParams), c_void_p, c_size_t, c_void_p]),
     "gorgon_verify_noalloc": (c_int, [POINTER(VerifyParams), c_void_p]),
     "gorgon_kv_trim": (c_int, [POINTER(KvTrimParams), c_void_p]),
+    "gorgon_candidate_tree_workspace_size": (c_size_t, [POINTER(CandidateTreeParams)]),
+    "gorgon_candidate_tree": (c_int, [POINTER(CandidateTreeParams), c_void_p, c_size_t, c_void_p]),
 }
 
 _lib = None

@@ -21,7 +21,7 @@ LIB = LIBDIR / "libgorgon_b200.so"
 INCLUDE = PKG.parent / "include"
 
 SOURCES = ["abi.cu", "tree_mask.cu", "attn_api.cu", "attn_simt.cu", "attn_tc.cu",
-           "verify.cu", "kv_trim.cu"]
+           "verify.cu", "kv_trim.cu", "cand_tree.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",

@@ -1,0 +1,531 @@
+// Candidate-tree builder on the device: the per-head statistics and the tree
+// assembly of build_candidate_tree (src/gorgon/inference/tree_candidates.py:
+// 92-245, with _topk_per_head :42-81) for a batch of sequences, with no host
+// synchronisation.  The reference runs both on the host: one softmax, one
+// entropy `.item()` and one top-k per head, then Python loops over the nodes.
+//
+// cand_stats_kernel — one CTA per (sequence, level) row of logits.  One pass
+//   over the vocabulary with 16-byte loads; every thread keeps an online
+//   (max m, Z = sum e^(x-m), T = sum e^(x-m) (x-m)) and its own top-K list
+//   (K = the list size the launch picked, >= top_k).  The CTA merges them:
+//   entropy = ln Z - T / Z, the top_k largest logits (descending; equal values
+//   by ascending id, a total order independent of the thread layout) and the
+//   softmax over those top_k logits.
+// cand_tree_kernel — one warp per sequence.  The reference's expansion, level
+//   by level: a level's (parent, candidate) pairs are taken in the reference's
+//   order (parents sorted by their own logit, descending and stable, when a
+//   budget is set; candidates in top-k order), 32 at a time; each lane tests
+//   its pair against the thresholds, a ballot gives every passing pair its
+//   rank, and pairs are kept while the budget lasts.  Path probabilities and
+//   thresholds are in double precision, as the reference's Python floats.
+#include <climits>
+#include <cmath>
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace gorgon {
+
+constexpr uint32_t kErrCandCapacity = 1u << 3;
+
+namespace {
+
+// Threads per statistics CTA: fewer for the 32-entry lists, whose registers
+// would otherwise spill.
+template <int K>
+struct StatCfg {
+  static constexpr int kThreads = K <= 16 ? 512 : 256;
+  static constexpr int kWarps = kThreads / 32;
+};
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct CandArgs {
+  const void* logits;
+  int64_t lsb, lsl;
+  int batch, levels, vocab, top_k, kk;  // kk = min(top_k, vocab)
+  int max_candidates;
+  double threshold;
+  int use_path, entropy_weighted;
+  int cap;
+  int64_t* tokens;
+  int32_t* parents;
+  float* probs;
+  int32_t* n_nodes;
+  int32_t* topk_ids;
+  float* topk_scores;
+  float* topk_probs;
+  float* entropy;
+  uint32_t* err;
+};
+
+// Strict total order of (value, id): larger value first, equal values by
+// smaller id; an empty slot (id < 0) comes last.
+__device__ __forceinline__ bool ahead(float a, int ia, float b, int ib) {
+  if (ib < 0) return ia >= 0;
+  if (ia < 0) return false;
+  return a > b || (a == b && ia < ib);
+}
+
+// Inserts (v, id) into a sorted register list of K entries (the last drops out).
+template <int K>
+__device__ __forceinline__ void list_insert(float (&kv)[K], int (&ki)[K], float v, int id) {
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const bool take = ahead(v, id, kv[j], ki[j]);
+    const float tv = kv[j];
+    const int ti = ki[j];
+    kv[j] = take ? v : tv;
+    ki[j] = take ? id : ti;
+    v = take ? tv : v;
+    id = take ? ti : id;
+  }
+}
+
+// Merges the 32 lanes' sorted lists into the first K entries of the order,
+// returned in lane 0's list (the other lanes' lists are consumed).
+template <int K>
+__device__ __forceinline__ void warp_merge(float (&kv)[K], int (&ki)[K]) {
+  const int lane = threadIdx.x & 31;
+  float ov[K];
+  int oi[K];
+#pragma unroll
+  for (int r = 0; r < K; ++r) {
+    float bv = kv[0];
+    int bi = ki[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ahead(v2, i2, bv, bi)) {
+        bv = v2;
+        bi = i2;
+      }
+    }
+    ov[r] = bv;
+    oi[r] = bi;
+    // the lane whose head won pops it (ids are unique, so exactly one lane)
+    if (bi >= 0 && ki[0] == bi) {
+#pragma unroll
+      for (int j = 0; j + 1 < K; ++j) {
+        kv[j] = kv[j + 1];
+        ki[j] = ki[j + 1];
+      }
+      kv[K - 1] = -INFINITY;
+      ki[K - 1] = -1;
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < K; ++r) {
+      kv[r] = ov[r];
+      ki[r] = oi[r];
+    }
+  }
+}
+
+// Online softmax statistics of one thread.
+struct Stats {
+  float m = -INFINITY, z = 0.f, t = 0.f;
+  __device__ __forceinline__ void rebase(float nm) {  // nm >= m
+    if (z > 0.f) {
+      const float d = m - nm;
+      const float c = sm100::ex2_approx(d * kLog2e);
+      t = c * (t + z * d);
+      z *= c;
+    }
+    m = nm;
+  }
+  __device__ __forceinline__ void add(float x) {
+    const float d = fmaxf(x - m, -1e30f);  // -inf logits add nothing (and no 0 * inf)
+    const float e = sm100::ex2_approx(d * kLog2e);
+    z += e;
+    t = fmaf(e, d, t);
+  }
+  __device__ __forceinline__ void merge(const Stats& o) {
+    if (o.z <= 0.f) return;
+    if (z <= 0.f) {
+      *this = o;
+      return;
+    }
+    const float nm = fmaxf(m, o.m);
+    const float d1 = m - nm, d2 = o.m - nm;
+    const float c1 = sm100::ex2_approx(d1 * kLog2e), c2 = sm100::ex2_approx(d2 * kLog2e);
+    t = c1 * (t + z * d1) + c2 * (o.t + o.z * d2);
+    z = c1 * z + c2 * o.z;
+    m = nm;
+  }
+};
+
+template <typename T, int K>
+__global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const CandArgs a) {
+  constexpr int kStatThreads = StatCfg<K>::kThreads;
+  constexpr int kStatWarps = StatCfg<K>::kWarps;
+  const int row = blockIdx.x;  // b * levels + l
+  const int b = row / a.levels, l = row - b * a.levels;
+  const T* src = static_cast<const T*>(a.logits) + static_cast<int64_t>(b) * a.lsb + static_cast<int64_t>(l) * a.lsl;
+  const int V = a.vocab;
+  Stats st;
+  float kv[K];
+  int ki[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = -INFINITY;
+    ki[j] = -1;
+  }
+  // A chunk of consecutive logits: one rebase of the running max, then every value.
+  auto chunk = [&](auto n_tag, const float* x, int id0) {
+    constexpr int N = decltype(n_tag)::value;
+    float cm = x[0];
+#pragma unroll
+    for (int j = 1; j < N; ++j) cm = fmaxf(cm, x[j]);
+    if (cm > st.m) st.rebase(cm);
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      st.add(x[j]);
+      if (ki[K - 1] < 0 || x[j] > kv[K - 1]) list_insert<K>(kv, ki, x[j], id0 + j);
+    }
+  };
+  constexpr int kVec = 16 / sizeof(T);
+  constexpr int kUnroll = 4;  // 16-byte loads in flight per thread
+  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
+  const int nvec = vec ? V / kVec : 0;
+  const uint4* src4 = reinterpret_cast<const uint4*>(src);
+  int v = threadIdx.x;
+  for (; v + (kUnroll - 1) * kStatThreads < nvec; v += kUnroll * kStatThreads) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) raw[u] = __ldg(src4 + v + u * kStatThreads);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const T* e = reinterpret_cast<const T*>(&raw[u]);
+      float x[kVec];
+#pragma unroll
+      for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
+      chunk(std::integral_constant<int, kVec>(), x, (v + u * kStatThreads) * kVec);
+    }
+  }
+  for (; v < nvec; v += kStatThreads) {
+    const uint4 raw = __ldg(src4 + v);
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float x[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
+    chunk(std::integral_constant<int, kVec>(), x, v * kVec);
+  }
+  for (int i = nvec * kVec + threadIdx.x; i < V; i += kStatThreads) {
+    const float x = Cvt<T>::to_f(src[i]);
+    chunk(std::integral_constant<int, 1>(), &x, i);
+  }
+
+  // ---- CTA merge: statistics through shuffles + shared memory, lists per warp then across warps
+  __shared__ float s_m[kStatWarps], s_z[kStatWarps], s_t[kStatWarps];
+  __shared__ float s_kv[kStatWarps][K];
+  __shared__ int s_ki[kStatWarps][K];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Stats other;
+    other.m = __shfl_xor_sync(0xffffffffu, st.m, o);
+    other.z = __shfl_xor_sync(0xffffffffu, st.z, o);
+    other.t = __shfl_xor_sync(0xffffffffu, st.t, o);
+    st.merge(other);
+  }
+  warp_merge<K>(kv, ki);
+  if (lane == 0) {
+    s_m[warp] = st.m;
+    s_z[warp] = st.z;
+    s_t[warp] = st.t;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      s_kv[warp][j] = kv[j];
+      s_ki[warp][j] = ki[j];
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  Stats all;
+  if (lane < kStatWarps) {
+    all.m = s_m[lane];
+    all.z = s_z[lane];
+    all.t = s_t[lane];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Stats other;
+    other.m = __shfl_xor_sync(0xffffffffu, all.m, o);
+    other.z = __shfl_xor_sync(0xffffffffu, all.z, o);
+    other.t = __shfl_xor_sync(0xffffffffu, all.t, o);
+    all.merge(other);
+  }
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = lane < kStatWarps ? s_kv[lane][j] : -INFINITY;
+    ki[j] = lane < kStatWarps ? s_ki[lane][j] : -1;
+  }
+  warp_merge<K>(kv, ki);
+  // lane 0 holds the top K; hand entry j to lane j
+  float myv = -INFINITY;
+  int myi = -1;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const float v = __shfl_sync(0xffffffffu, kv[j], 0);
+    const int i = __shfl_sync(0xffffffffu, ki[j], 0);
+    if (lane == j) {
+      myv = v;
+      myi = i;
+    }
+  }
+  const float top = __shfl_sync(0xffffffffu, myv, 0);
+  const bool mine = lane < a.kk;
+  // softmax over the kept logits, relative to the largest
+  const float e = mine ? expf(myv - top) : 0.f;
+  const float es = warp_sum(e);
+  const int64_t o = static_cast<int64_t>(row) * a.top_k + lane;
+  if (mine) {
+    a.topk_ids[o] = myi;
+    a.topk_scores[o] = myv;
+    a.topk_probs[o] = e / es;
+  } else if (lane < a.top_k) {  // top_k above the vocabulary: empty slots
+    a.topk_ids[o] = -1;
+    a.topk_scores[o] = -INFINITY;
+    a.topk_probs[o] = 0.f;
+  }
+  if (lane == 0) a.entropy[row] = all.z > 0.f ? logf(all.z) - all.t / all.z : 0.f;
+}
+
+__device__ __forceinline__ unsigned lanes_below() {
+  unsigned r;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(r));
+  return r;
+}
+
+// One warp builds one sequence's tree.  Shared memory: path probability per
+// node, the current and next level's (node, logit) lists, and the expansion
+// order of the current level.
+__global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int cap = a.cap;
+  double* path = reinterpret_cast<double*>(smem);
+  int* lvl_node = reinterpret_cast<int*>(path + cap);               // [2][cap]
+  float* lvl_score = reinterpret_cast<float*>(lvl_node + 2 * cap);  // [2][cap]
+  int* order = reinterpret_cast<int*>(lvl_score + 2 * cap);         // [cap]
+  const int b = blockIdx.x, lane = threadIdx.x;
+  const int K = a.kk;
+  const bool thr_on = a.threshold > 0.0;
+  int64_t* tokens = a.tokens + static_cast<int64_t>(b) * cap;
+  int32_t* parents = a.parents + static_cast<int64_t>(b) * cap;
+  float* probs = a.probs + static_cast<int64_t>(b) * cap;
+  // the level's threshold: scaled by 1 - entropy / ln(top_k) when entropy-weighted
+  auto level_threshold = [&](int l) -> double {
+    if (thr_on && a.entropy_weighted) {
+      const double max_ent = a.top_k > 1 ? log(static_cast<double>(a.top_k)) : 1.0;
+      const double ent = static_cast<double>(a.entropy[static_cast<int64_t>(b) * a.levels + l]);
+      return a.threshold * (1.0 - ent / max_ent);
+    }
+    return a.threshold;
+  };
+  int n = 0;  // nodes so far
+  int budget = a.max_candidates < 0 ? INT_MAX : a.max_candidates;
+  bool overflow = false;  // the capacity, not the budget, cut a level
+  // Keeps the passing pairs of one 32-pair chunk, in lane order, while the
+  // budget and the capacity last.  Returns how many were kept; `slot` is this
+  // lane's rank among them (-1 if its pair is not kept).
+  auto take = [&](bool pass, int& slot) -> int {
+    const unsigned bal = __ballot_sync(0xffffffffu, pass);
+    const int pos = __popc(bal & lanes_below());
+    const int want = __popc(bal);
+    const int room = cap - n;
+    const int lim = budget < room ? budget : room;
+    if (want > lim && room < budget) overflow = true;
+    slot = (pass && pos < lim) ? pos : -1;
+    const int cnt = want < lim ? want : lim;
+    n += cnt;
+    budget -= cnt;
+    return cnt;
+  };
+
+  // ---- level 0: head 0's candidates become roots (tree_candidates.py:149-172)
+  int cur = 0, cur_n = 0;
+  {
+    const double thr = level_threshold(0);
+    const int64_t s0 = static_cast<int64_t>(b) * a.levels * a.top_k;
+    for (int base = 0; base < K && budget > 0; base += 32) {
+      const int i = base + lane;
+      const bool valid = i < K;
+      const float pr = valid ? a.topk_probs[s0 + i] : 0.f;
+      const bool pass = valid && !(thr_on && static_cast<double>(pr) < thr);
+      const int n0 = n;
+      int slot;
+      const int cnt = take(pass, slot);
+      if (slot >= 0) {
+        const int node = n0 + slot;
+        tokens[node] = a.topk_ids[s0 + i];
+        parents[node] = -1;
+        probs[node] = pr;
+        path[node] = static_cast<double>(pr);
+        lvl_node[cur * cap + cur_n + slot] = node;
+        lvl_score[cur * cap + cur_n + slot] = a.topk_scores[s0 + i];
+      }
+      cur_n += cnt;
+    }
+  }
+  __syncwarp();
+
+  // ---- later levels: every node of the level above x the level's candidates (:175-226)
+  for (int l = 1; l < a.levels && budget > 0; ++l) {
+    const double thr = level_threshold(l);
+    const int64_t sl = (static_cast<int64_t>(b) * a.levels + l) * a.top_k;
+    // expansion order: by the parent's own logit, descending and stable, under a budget
+    for (int p = lane; p < cur_n; p += 32) {
+      int rank = p;
+      if (a.max_candidates >= 0) {
+        const float sp = lvl_score[cur * cap + p];
+        rank = 0;
+        for (int q = 0; q < cur_n; ++q) {
+          const float sq = lvl_score[cur * cap + q];
+          rank += (sq > sp || (sq == sp && q < p)) ? 1 : 0;
+        }
+      }
+      order[rank] = p;
+    }
+    __syncwarp();
+    const int nxt = cur ^ 1;
+    int nxt_n = 0;
+    const int total = cur_n * K;
+    for (int base = 0; base < total && budget > 0; base += 32) {
+      const int j = base + lane;
+      const bool valid = j < total;
+      int i = 0, pnode = 0;
+      float pr = 0.f;
+      double cp = 0.0;
+      if (valid) {
+        const int pj = j / K;
+        i = j - pj * K;
+        pnode = lvl_node[cur * cap + order[pj]];
+        pr = a.topk_probs[sl + i];
+        cp = path[pnode] * static_cast<double>(pr);
+      }
+      const bool pass = valid && !(thr_on && static_cast<double>(pr) < thr) &&
+                        !(a.use_path && thr_on && cp < thr);
+      const int n0 = n;
+      int slot;
+      const int cnt = take(pass, slot);
+      if (slot >= 0) {
+        const int node = n0 + slot;
+        tokens[node] = a.topk_ids[sl + i];
+        parents[node] = pnode;
+        probs[node] = pr;
+        path[node] = cp;
+        lvl_node[nxt * cap + nxt_n + slot] = node;
+        lvl_score[nxt * cap + nxt_n + slot] = a.topk_scores[sl + i];
+      }
+      nxt_n += cnt;
+    }
+    __syncwarp();
+    cur = nxt;
+    cur_n = nxt_n;
+  }
+
+  if (lane == 0) {
+    a.n_nodes[b] = n;
+    if (overflow) raise_device_error(a.err, kErrCandCapacity);
+  }
+  for (int s = n + lane; s < cap; s += 32) {
+    tokens[s] = -1;
+    parents[s] = -1;
+    probs[s] = 0.f;
+  }
+}
+
+template <typename T>
+int launch_stats_t(const CandArgs& a, int kmax, int rows, cudaStream_t st) {
+  if (kmax <= 4) cand_stats_kernel<T, 4><<<rows, StatCfg<4>::kThreads, 0, st>>>(a);
+  else if (kmax <= 8) cand_stats_kernel<T, 8><<<rows, StatCfg<8>::kThreads, 0, st>>>(a);
+  else if (kmax <= 16) cand_stats_kernel<T, 16><<<rows, StatCfg<16>::kThreads, 0, st>>>(a);
+  else cand_stats_kernel<T, 32><<<rows, StatCfg<32>::kThreads, 0, st>>>(a);
+  return check_cuda(cudaGetLastError(), "candidate-tree statistics launch");
+}
+
+constexpr size_t kWsAlign = 256;
+inline size_t ws_align(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
+
+}  // namespace
+}  // namespace gorgon
+
+extern "C" size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tree_params* p) {
+  using namespace gorgon;
+  if (!p || p->batch <= 0 || p->levels <= 0 || p->top_k <= 0) return 0;
+  const size_t rows = static_cast<size_t>(p->batch) * static_cast<size_t>(p->levels);
+  const size_t per = rows * static_cast<size_t>(p->top_k);
+  return ws_align(per * sizeof(int32_t)) + 2 * ws_align(per * sizeof(float)) + ws_align(rows * sizeof(float));
+}
+
+extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  using namespace gorgon;
+  if (!p) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: params is null");
+  if (!dtype_ok(p->dtype)) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: unknown dtype");
+  if (p->batch < 0 || p->levels < 0 || p->vocab < 0)
+    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: negative size");
+  if (p->batch == 0) return GORGON_OK;
+  if (p->levels < 1) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: levels must be >= 1");
+  if (p->vocab < 1 || p->vocab > INT_MAX - 16)
+    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: vocab outside [1, 2^31)");
+  if (p->top_k < 1 || p->top_k > 32)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: top_k must be in [1, 32]");
+  if (p->max_nodes < 1 || p->max_nodes > 4096)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: max_nodes must be in [1, 4096]");
+  if (p->batch > INT_MAX / p->levels || p->batch > 2147483647LL)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: batch * levels too large");
+  if (!(p->confidence_threshold == p->confidence_threshold))
+    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: confidence_threshold is NaN");
+  if (!p->logits || !p->tokens || !p->parents || !p->probs || !p->n_nodes)
+    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: null pointer");
+  const size_t need = gorgon_candidate_tree_workspace_size(p);
+  const bool all_stats = p->topk_ids && p->topk_scores && p->topk_probs && p->entropy;
+  if (!all_stats && (!workspace || workspace_bytes < need))
+    return set_error(GORGON_ERR_WORKSPACE, "gorgon_candidate_tree: workspace too small");
+  const int rows = static_cast<int>(p->batch * p->levels);
+  const size_t per = static_cast<size_t>(rows) * static_cast<size_t>(p->top_k);
+  char* ws = static_cast<char*>(workspace);
+  CandArgs a{};
+  a.logits = p->logits;
+  a.lsb = p->logits_stride_b;
+  a.lsl = p->logits_stride_l;
+  a.batch = static_cast<int>(p->batch);
+  a.levels = static_cast<int>(p->levels);
+  a.vocab = static_cast<int>(p->vocab);
+  a.top_k = p->top_k;
+  a.kk = static_cast<int>(p->vocab < p->top_k ? p->vocab : p->top_k);
+  a.max_candidates = p->max_candidates;
+  a.threshold = static_cast<double>(p->confidence_threshold);
+  a.use_path = p->use_path_confidence != 0;
+  a.entropy_weighted = p->entropy_weighted != 0;
+  a.cap = static_cast<int>(p->max_nodes);
+  a.tokens = p->tokens;
+  a.parents = p->parents;
+  a.probs = p->probs;
+  a.n_nodes = p->n_nodes;
+  a.topk_ids = p->topk_ids ? p->topk_ids : reinterpret_cast<int32_t*>(ws);
+  a.topk_scores = p->topk_scores ? p->topk_scores : reinterpret_cast<float*>(ws + ws_align(per * 4));
+  a.topk_probs = p->topk_probs ? p->topk_probs : reinterpret_cast<float*>(ws + ws_align(per * 4) + ws_align(per * 4));
+  a.entropy = p->entropy ? p->entropy
+                         : reinterpret_cast<float*>(ws + ws_align(per * 4) + 2 * ws_align(per * 4));
+  a.err = device_error_word();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (p->dtype == GORGON_F32) rc = launch_stats_t<float>(a, a.kk, rows, st);
+  else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, a.kk, rows, st);
+  else rc = launch_stats_t<__half>(a, a.kk, rows, st);
+  if (rc) return rc;
+  const size_t smem = static_cast<size_t>(a.cap) * (sizeof(double) + 2 * sizeof(int) + 2 * sizeof(float) + sizeof(int));
+  if (smem > 48 * 1024) {
+    rc = check_cuda(cudaFuncSetAttribute(cand_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)),
+                    "candidate-tree smem attribute");
+    if (rc) return rc;
+  }
+  cand_tree_kernel<<<static_cast<unsigned>(p->batch), 32, smem, st>>>(a);
+  return check_cuda(cudaGetLastError(), "candidate-tree launch");
+}
