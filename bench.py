@@ -79,6 +79,10 @@ WORKLOADS = {
     # multi-pass profiler capture; its traffic scales with the layer count
     "kvtrim-b32-l4-p4096": dict(kind="trim", B=32, layers=4, Hkv=8, D=128, P=4096, N=64, dtype="bf16",
                                 max_depth=5),
+    # candidate trees from 4 Medusa heads over a 128256-token vocabulary:
+    # per-head top-4, softmax and entropy, then a 64-node budgeted tree
+    "candidates-b32-h4-v128256": dict(kind="cand", B=32, heads=4, V=128256, top_k=4, max_candidates=64,
+                                      dtype="bf16"),
 }
 DEFAULT_WORKLOAD = "verify-b16-p8192-n64"
 TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
@@ -430,9 +434,91 @@ class TrimWorkload:
                            f"{cfg['B']} sequences")}
 
 
+class CandidateWorkload:
+    """Candidate-tree construction for a batch (gorgon_candidate_tree): the
+    Medusa heads' logits [B, heads, V] bf16 ~ N(0, 2) are read once for every
+    head's top-k, softmax and entropy, then each sequence's tree is assembled
+    under the node budget."""
+
+    metric = "candidate-tree builder HBM GB/s (logits bytes / step time)"
+    data = "synthetic (seeded N(0,2) bf16 head logits)"
+    bound = "hbm"
+    flush_l2 = True  # 33 MB of logits fit in L2
+
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
+        cfg = WORKLOADS[name]
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, L, V = cfg["B"], cfg["heads"], cfg["V"]
+        self.logits = torch.empty(B, L, V, device=dev, dtype=torch.bfloat16)
+        for j in range(B):
+            _fill_normal(self.logits[j], torch.Generator(device=dev).manual_seed(4_000_003 + first_seq + j), 2.0)
+        self.cap = G.inference.max_tree_nodes(cfg["top_k"], L, V, cfg["max_candidates"])
+        self.bytes = B * L * V * 2 + B * (self.cap * (8 + 4 + 4) + 4)  # logits in; tokens, parents, probs, count out
+        self.flops = 0
+        self.tokens = B * self.cap
+
+    def step(self):
+        c = self.cfg
+        return G.build_candidate_trees(self.logits, top_k=c["top_k"], max_candidates=c["max_candidates"])
+
+    def plan(self):
+        return {"backend": "cand_stats_kernel", "splits": None, "launches": 2}
+
+    def config(self, world: int, plan: dict) -> dict:
+        c = self.cfg
+        return {"workload": self.name, "batch_per_gpu": c["B"], "heads": c["heads"], "vocab": c["V"],
+                "top_k": c["top_k"], "max_candidates": c["max_candidates"], "logits_dtype": "bf16",
+                "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                "l2": "L2 flushed before every step (a 256 MB write outside the step's events)",
+                "backend": plan["backend"]}
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        return {"us_per_step": round(ms_step * 1e3, 2),
+                "trees_built_per_s": round(world * self.cfg["B"] / (ms_step * 1e-3), 1)}
+
+    def e2e(self, steps: int, warmup: int, world: int):
+        """Each step: the trees built and their tokens, parents and node
+        counts copied to pinned host memory (the logits stay on the device,
+        where the heads wrote them)."""
+        dev, B = self.dev, self.cfg["B"]
+        tok_h = torch.empty(B, self.cap, dtype=torch.int64).pin_memory()
+        par_h = torch.empty(B, self.cap, dtype=torch.int32).pin_memory()
+        n_h = torch.empty(B, dtype=torch.int32).pin_memory()
+        d2h = tok_h.numel() * 8 + par_h.numel() * 4 + n_h.numel() * 4
+
+        def one():
+            t = self.step()
+            tok_h.copy_(t.tokens, non_blocking=True)
+            par_h.copy_(t.parents, non_blocking=True)
+            n_h.copy_(t.n_nodes, non_blocking=True)
+
+        ms = _time_loop(one, dev, steps, warmup, world)
+        return ms, 0, d2h, "head logits resident in HBM (written there by the heads); trees out to the host"
+
+    def cpu_baseline(self, budget_s: float):
+        from oracle import gorgon_oracle as O
+        c = self.cfg
+        times = []
+        t_start = time.perf_counter()
+        for j in range(c["B"]):
+            lg = self.logits[j].float().cpu().numpy()
+            t0 = time.perf_counter()
+            levels = [O.head_topk(lg[h], c["top_k"]) for h in range(c["heads"])]
+            O.build_candidate_tree(levels, c["top_k"], max_candidates=c["max_candidates"])
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+        step_s = float(np.mean(times)) * c["B"]
+        return {"value": round(self.bytes / step_s / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                "us_per_step": round(step_s * 1e6, 1),
+                "sample": (f"{len(times)} of {c['B']} sequences through the oracle's head_topk (per head: "
+                           f"top-k, softmax, entropy) and build_candidate_tree, extrapolated to the batch")}
+
+
 def make_workload(name: str, dev: torch.device, first_seq: int = 0):
     kind = WORKLOADS[name].get("kind", "attn")
-    return {"attn": Workload, "verify": VerifyWorkload, "trim": TrimWorkload}[kind](name, dev, first_seq)
+    return {"attn": Workload, "verify": VerifyWorkload, "trim": TrimWorkload,
+            "cand": CandidateWorkload}[kind](name, dev, first_seq)
 
 
 # --------------------------------------------------------------------------
@@ -590,7 +676,12 @@ def dist_setup():
 
 
 def time_device(wl: Workload, steps: int, warmup: int, world: int):
+    """(ms of the timed steps, mean ms per step, clock summary).  A workload
+    whose inputs fit in L2 sets ``flush_l2``: a 256 MB write then evicts L2
+    before every step, outside the step's events, and the time is the sum of
+    the steps' own event times."""
     dev = wl.dev
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if getattr(wl, "flush_l2", False) else None
     for _ in range(warmup):
         wl.step()
     torch.cuda.synchronize(dev)
@@ -602,12 +693,16 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     with ClockSampler(dev) as clk:
         for i in range(steps):
+            if flush is not None:
+                flush.fill_(i & 0xff)
             starts[i].record(st)
             wl.step()
             ends[i].record(st)
         torch.cuda.synchronize(dev)
     total_ms = starts[0].elapsed_time(ends[-1])
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    if flush is not None:
+        total_ms = float(np.sum(per))
     if world > 1:
         torch.distributed.barrier()
     return total_ms, float(np.mean(per)), clk.summary()
@@ -849,15 +944,30 @@ def run_reference(args):
 
 
 def run_reference_other(args, cfg: dict, world: int):
-    """Reference arm of the verifier and trim workloads: the oracle's
-    verify_tree (one sequence per step) or kv_trim (one layer of four
-    sequences per step, the reference's clone + gather) on host-generated
-    inputs of the workload's shapes, extrapolated to the whole step."""
+    """Reference arm of the verifier, trim and candidate-tree workloads: the
+    oracle's verify_tree (one sequence per step), kv_trim (one layer of four
+    sequences per step, the reference's clone + gather) or head_topk +
+    build_candidate_tree (one sequence per step) on host-generated inputs of
+    the workload's shapes, extrapolated to the whole step."""
     from oracle import gorgon_oracle as O
     rng = np.random.default_rng(0)
     prng = random.Random(0)
-    B, N = cfg["B"], cfg["N"]
-    if cfg["kind"] == "verify":
+    B, N = cfg["B"], cfg.get("N", 0)
+    if cfg["kind"] == "cand":
+        L, V, k, mc = cfg["heads"], cfg["V"], cfg["top_k"], cfg["max_candidates"]
+        cap = min(sum(k ** (i + 1) for i in range(L)), mc)
+        wl_bytes = B * L * V * 2 + B * (cap * 16 + 4)
+        metric, what = CandidateWorkload.metric, ("one sequence through the oracle's head_topk and "
+                                                  "build_candidate_tree, x batch")
+
+        def sample():
+            return rng.standard_normal((L, V), dtype=np.float32) * 2.0
+
+        def run(s):
+            levels = [O.head_topk(s[h], k) for h in range(L)]
+            O.build_candidate_tree(levels, k, max_candidates=mc)
+        scale = B
+    elif cfg["kind"] == "verify":
         V, R = cfg["V"], cfg["N"] + 1
         wl_bytes = B * R * V * 2 + 2 * B * N * 4 + B * (R * 4 + N * 4 + 16)
         metric, what = VerifyWorkload.metric, "one sequence through the oracle's verify_tree, x batch"

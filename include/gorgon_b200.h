@@ -262,7 +262,7 @@ GORGON_API int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream);
  * non-NULL (the workspace holds them otherwise).  The entropy is
  * ln Z - sum(e^x (x - max)) / Z, the reference's -sum p log(p + 1e-10)
  * without the 1e-10 (at most ~1e-5 apart for a 128k vocabulary).
- * top_k <= 32, max_nodes <= 4096.
+ * top_k <= 32, levels <= 64, max_nodes <= 4096.
  * ---------------------------------------------------------------------- */
 typedef struct {
   int32_t dtype;  /* gorgon_dtype of logits */

@@ -4,13 +4,17 @@
 // synchronisation.  The reference runs both on the host: one softmax, one
 // entropy `.item()` and one top-k per head, then Python loops over the nodes.
 //
-// cand_stats_kernel — one CTA per (sequence, level) row of logits.  One pass
-//   over the vocabulary with 16-byte loads; every thread keeps an online
-//   (max m, Z = sum e^(x-m), T = sum e^(x-m) (x-m)) and its own top-K list
-//   (K = the list size the launch picked, >= top_k).  The CTA merges them:
-//   entropy = ln Z - T / Z, the top_k largest logits (descending; equal values
-//   by ascending id, a total order independent of the thread layout) and the
-//   softmax over those top_k logits.
+// cand_stats_kernel — one CTA per (sequence, level) row of logits.  Pass 1
+//   reads the row from HBM (16-byte loads, 8 in flight per thread): every
+//   thread keeps an online (max m, Z = sum e^(x-m), T = sum e^(x-m) (x-m))
+//   and its own maximum; entropy = ln Z - T / Z.  A bound follows from the
+//   thread maxima: warp w's k-th largest leaves k logits at or above it, so
+//   the row's top k are all >= the largest such value.  Pass 2 re-reads the
+//   row (now in L2) and appends every logit at or above the bound to a
+//   shared-memory buffer, from which one warp picks the top k (descending;
+//   equal values by ascending id, a total order independent of the thread
+//   layout) and their softmax.  Rows with more ties at the bound than the
+//   buffer holds take a third pass with per-thread top-K lists instead.
 // cand_tree_kernel — one warp per sequence.  The reference's expansion, level
 //   by level: a level's (parent, candidate) pairs are taken in the reference's
 //   order (parents sorted by their own logit, descending and stable, when a
@@ -157,72 +161,102 @@ struct Stats {
   }
 };
 
-template <typename T, int K>
-__global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const CandArgs a) {
-  constexpr int kStatThreads = StatCfg<K>::kThreads;
-  constexpr int kStatWarps = StatCfg<K>::kWarps;
-  const int row = blockIdx.x;  // b * levels + l
-  const int b = row / a.levels, l = row - b * a.levels;
-  const T* src = static_cast<const T*>(a.logits) + static_cast<int64_t>(b) * a.lsb + static_cast<int64_t>(l) * a.lsl;
-  const int V = a.vocab;
-  Stats st;
-  float kv[K];
-  int ki[K];
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
-    kv[j] = -INFINITY;
-    ki[j] = -1;
-  }
-  // A chunk of consecutive logits: one rebase of the running max, then every value.
-  auto chunk = [&](auto n_tag, const float* x, int id0) {
-    constexpr int N = decltype(n_tag)::value;
-    float cm = x[0];
-#pragma unroll
-    for (int j = 1; j < N; ++j) cm = fmaxf(cm, x[j]);
-    if (cm > st.m) st.rebase(cm);
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      st.add(x[j]);
-      if (ki[K - 1] < 0 || x[j] > kv[K - 1]) list_insert<K>(kv, ki, x[j], id0 + j);
-    }
-  };
+// 16-byte streaming load that the compiler keeps where it is written, so a
+// batch of them is in flight before the first is used.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Visits a row's logits as 16-byte vectors (8 in flight per thread), then the
+// scalar remainder, calling f(count tag, x[], first id) per vector or value.
+template <typename T, int NT, typename F>
+__device__ __forceinline__ void for_row(const T* src, int V, F&& f) {
   constexpr int kVec = 16 / sizeof(T);
-  constexpr int kUnroll = 4;  // 16-byte loads in flight per thread
+  constexpr int kUnroll = 8;
   const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
   const int nvec = vec ? V / kVec : 0;
   const uint4* src4 = reinterpret_cast<const uint4*>(src);
   int v = threadIdx.x;
-  for (; v + (kUnroll - 1) * kStatThreads < nvec; v += kUnroll * kStatThreads) {
+  for (; v + (kUnroll - 1) * NT < nvec; v += kUnroll * NT) {
     uint4 raw[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) raw[u] = __ldg(src4 + v + u * kStatThreads);
+    for (int u = 0; u < kUnroll; ++u) raw[u] = ld_stream(src4 + v + u * NT);
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const T* e = reinterpret_cast<const T*>(&raw[u]);
       float x[kVec];
 #pragma unroll
       for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
-      chunk(std::integral_constant<int, kVec>(), x, (v + u * kStatThreads) * kVec);
+      f(std::integral_constant<int, kVec>(), x, (v + u * NT) * kVec);
     }
   }
-  for (; v < nvec; v += kStatThreads) {
-    const uint4 raw = __ldg(src4 + v);
+  for (; v < nvec; v += NT) {
+    const uint4 raw = ld_stream(src4 + v);
     const T* e = reinterpret_cast<const T*>(&raw);
     float x[kVec];
 #pragma unroll
     for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
-    chunk(std::integral_constant<int, kVec>(), x, v * kVec);
+    f(std::integral_constant<int, kVec>(), x, v * kVec);
   }
-  for (int i = nvec * kVec + threadIdx.x; i < V; i += kStatThreads) {
+  for (int i = nvec * kVec + threadIdx.x; i < V; i += NT) {
     const float x = Cvt<T>::to_f(src[i]);
-    chunk(std::integral_constant<int, 1>(), &x, i);
+    f(std::integral_constant<int, 1>(), &x, i);
   }
+}
 
-  // ---- CTA merge: statistics through shuffles + shared memory, lists per warp then across warps
-  __shared__ float s_m[kStatWarps], s_z[kStatWarps], s_t[kStatWarps];
-  __shared__ float s_kv[kStatWarps][K];
-  __shared__ int s_ki[kStatWarps][K];
+// k-th largest (1 <= k <= 32) of the warp's 32 values: bitonic sort across
+// the lanes, descending, then lane k - 1's value.
+__device__ __forceinline__ float warp_kth_largest(float x, int k) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const float y = __shfl_xor_sync(0xffffffffu, x, stride);
+      const bool lower = (lane & stride) == 0;  // first lane of the compared pair
+      const bool desc = (lane & size) == 0;     // this run is sorted descending
+      x = (lower == desc) ? fmaxf(x, y) : fminf(x, y);
+    }
+  }
+  return __shfl_sync(0xffffffffu, x, k - 1);
+}
+
+constexpr int kCandBuf = 2048;  // logits at or above the bound kept per row
+
+template <typename T, int K>
+__global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const CandArgs a) {
+  constexpr int NT = StatCfg<K>::kThreads;
+  constexpr int NW = StatCfg<K>::kWarps;
+  const int row = blockIdx.x;  // b * levels + l
+  const int b = row / a.levels, l = row - b * a.levels;
+  const T* src = static_cast<const T*>(a.logits) + static_cast<int64_t>(b) * a.lsb + static_cast<int64_t>(l) * a.lsl;
+  const int V = a.vocab;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float s_m[NW], s_z[NW], s_t[NW], s_bound[NW];
+  __shared__ float s_kv[NW][K];
+  __shared__ int s_ki[NW][K];
+  __shared__ float s_bv[kCandBuf];
+  __shared__ int s_bi[kCandBuf];
+  __shared__ int s_count;
+  if (threadIdx.x == 0) s_count = 0;
+
+  // ---- pass 1 (HBM): online softmax statistics and this thread's maximum
+  Stats st;
+  float tmax = -INFINITY;
+  for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int) {
+    constexpr int N = decltype(n_tag)::value;
+    float cm = x[0];
+#pragma unroll
+    for (int j = 1; j < N; ++j) cm = fmaxf(cm, x[j]);
+    if (cm > st.m) st.rebase(cm);
+#pragma unroll
+    for (int j = 0; j < N; ++j) st.add(x[j]);
+    tmax = fmaxf(tmax, cm);
+  });
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     Stats other;
@@ -231,21 +265,79 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
     other.t = __shfl_xor_sync(0xffffffffu, st.t, o);
     st.merge(other);
   }
-  warp_merge<K>(kv, ki);
+  // warp w's kk-th largest thread maximum leaves kk logits of warp w at or
+  // above it (a thread without logits reports -inf)
+  const float wk = warp_kth_largest(tmax, a.kk);
   if (lane == 0) {
     s_m[warp] = st.m;
     s_z[warp] = st.z;
     s_t[warp] = st.t;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      s_kv[warp][j] = kv[j];
-      s_ki[warp][j] = ki[j];
-    }
+    s_bound[warp] = wk;
   }
   __syncthreads();
+  float bound = s_bound[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) bound = fmaxf(bound, s_bound[w]);
+
+  // ---- pass 2 (L2): every logit at or above the bound into the buffer
+  for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int id0) {
+    constexpr int N = decltype(n_tag)::value;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (x[j] >= bound) {
+        const int slot = atomicAdd(&s_count, 1);
+        if (slot < kCandBuf) {
+          s_bv[slot] = x[j];
+          s_bi[slot] = id0 + j;
+        }
+      }
+  });
+  __syncthreads();
+  const int count = s_count;
+
+  float kv[K];
+  int ki[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = -INFINITY;
+    ki[j] = -1;
+  }
+  if (count <= kCandBuf) {
+    if (warp == 0) {  // one warp picks the top K of the buffer
+      for (int j = lane; j < count; j += 32) list_insert<K>(kv, ki, s_bv[j], s_bi[j]);
+      warp_merge<K>(kv, ki);
+    }
+  } else {
+    // More ties at the bound than the buffer holds: exact per-thread lists
+    // over the row, filtered by the bound, merged per warp, then across warps.
+    for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int id0) {
+      constexpr int N = decltype(n_tag)::value;
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (x[j] >= bound && (ki[K - 1] < 0 || x[j] > kv[K - 1])) list_insert<K>(kv, ki, x[j], id0 + j);
+    });
+    warp_merge<K>(kv, ki);
+    if (lane == 0) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        s_kv[warp][j] = kv[j];
+        s_ki[warp][j] = ki[j];
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < K; ++j) {
+        kv[j] = lane < NW ? s_kv[lane][j] : -INFINITY;
+        ki[j] = lane < NW ? s_ki[lane][j] : -1;
+      }
+      warp_merge<K>(kv, ki);
+    }
+  }
   if (warp != 0) return;
+
   Stats all;
-  if (lane < kStatWarps) {
+  if (lane < NW) {
     all.m = s_m[lane];
     all.z = s_z[lane];
     all.t = s_t[lane];
@@ -258,12 +350,6 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
     other.t = __shfl_xor_sync(0xffffffffu, all.t, o);
     all.merge(other);
   }
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
-    kv[j] = lane < kStatWarps ? s_kv[lane][j] : -INFINITY;
-    ki[j] = lane < kStatWarps ? s_ki[lane][j] : -1;
-  }
-  warp_merge<K>(kv, ki);
   // lane 0 holds the top K; hand entry j to lane j
   float myv = -INFINITY;
   int myi = -1;
@@ -301,8 +387,9 @@ __device__ __forceinline__ unsigned lanes_below() {
 }
 
 // One warp builds one sequence's tree.  Shared memory: path probability per
-// node, the current and next level's (node, logit) lists, and the expansion
-// order of the current level.
+// node, the current and next level's (node, logit) lists, the expansion order
+// of the current level, and the sequence's per-level statistics (read once,
+// coalesced, so the level loops wait on no global load).
 __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int cap = a.cap;
@@ -310,7 +397,22 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   int* lvl_node = reinterpret_cast<int*>(path + cap);               // [2][cap]
   float* lvl_score = reinterpret_cast<float*>(lvl_node + 2 * cap);  // [2][cap]
   int* order = reinterpret_cast<int*>(lvl_score + 2 * cap);         // [cap]
+  const int LK = a.levels * a.top_k;
+  int* s_ids = order + cap;                                          // [levels][top_k]
+  float* s_score = reinterpret_cast<float*>(s_ids + LK);
+  float* s_prob = s_score + LK;
+  float* s_ent = s_prob + LK;                                        // [levels]
   const int b = blockIdx.x, lane = threadIdx.x;
+  {
+    const int64_t base = static_cast<int64_t>(b) * LK;
+    for (int j = lane; j < LK; j += 32) {
+      s_ids[j] = a.topk_ids[base + j];
+      s_score[j] = a.topk_scores[base + j];
+      s_prob[j] = a.topk_probs[base + j];
+    }
+    for (int j = lane; j < a.levels; j += 32) s_ent[j] = a.entropy[static_cast<int64_t>(b) * a.levels + j];
+    __syncwarp();
+  }
   const int K = a.kk;
   const bool thr_on = a.threshold > 0.0;
   int64_t* tokens = a.tokens + static_cast<int64_t>(b) * cap;
@@ -320,7 +422,7 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   auto level_threshold = [&](int l) -> double {
     if (thr_on && a.entropy_weighted) {
       const double max_ent = a.top_k > 1 ? log(static_cast<double>(a.top_k)) : 1.0;
-      const double ent = static_cast<double>(a.entropy[static_cast<int64_t>(b) * a.levels + l]);
+      const double ent = static_cast<double>(s_ent[l]);
       return a.threshold * (1.0 - ent / max_ent);
     }
     return a.threshold;
@@ -349,23 +451,23 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   int cur = 0, cur_n = 0;
   {
     const double thr = level_threshold(0);
-    const int64_t s0 = static_cast<int64_t>(b) * a.levels * a.top_k;
+    const int s0 = 0;
     for (int base = 0; base < K && budget > 0; base += 32) {
       const int i = base + lane;
       const bool valid = i < K;
-      const float pr = valid ? a.topk_probs[s0 + i] : 0.f;
+      const float pr = valid ? s_prob[s0 + i] : 0.f;
       const bool pass = valid && !(thr_on && static_cast<double>(pr) < thr);
       const int n0 = n;
       int slot;
       const int cnt = take(pass, slot);
       if (slot >= 0) {
         const int node = n0 + slot;
-        tokens[node] = a.topk_ids[s0 + i];
+        tokens[node] = s_ids[s0 + i];
         parents[node] = -1;
         probs[node] = pr;
         path[node] = static_cast<double>(pr);
         lvl_node[cur * cap + cur_n + slot] = node;
-        lvl_score[cur * cap + cur_n + slot] = a.topk_scores[s0 + i];
+        lvl_score[cur * cap + cur_n + slot] = s_score[s0 + i];
       }
       cur_n += cnt;
     }
@@ -375,7 +477,7 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   // ---- later levels: every node of the level above x the level's candidates (:175-226)
   for (int l = 1; l < a.levels && budget > 0; ++l) {
     const double thr = level_threshold(l);
-    const int64_t sl = (static_cast<int64_t>(b) * a.levels + l) * a.top_k;
+    const int sl = l * a.top_k;
     // expansion order: by the parent's own logit, descending and stable, under a budget
     for (int p = lane; p < cur_n; p += 32) {
       int rank = p;
@@ -403,7 +505,7 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
         const int pj = j / K;
         i = j - pj * K;
         pnode = lvl_node[cur * cap + order[pj]];
-        pr = a.topk_probs[sl + i];
+        pr = s_prob[sl + i];
         cp = path[pnode] * static_cast<double>(pr);
       }
       const bool pass = valid && !(thr_on && static_cast<double>(pr) < thr) &&
@@ -413,12 +515,12 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
       const int cnt = take(pass, slot);
       if (slot >= 0) {
         const int node = n0 + slot;
-        tokens[node] = a.topk_ids[sl + i];
+        tokens[node] = s_ids[sl + i];
         parents[node] = pnode;
         probs[node] = pr;
         path[node] = cp;
         lvl_node[nxt * cap + nxt_n + slot] = node;
-        lvl_score[nxt * cap + nxt_n + slot] = a.topk_scores[sl + i];
+        lvl_score[nxt * cap + nxt_n + slot] = s_score[sl + i];
       }
       nxt_n += cnt;
     }
@@ -476,7 +578,8 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
     return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: top_k must be in [1, 32]");
   if (p->max_nodes < 1 || p->max_nodes > 4096)
     return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: max_nodes must be in [1, 4096]");
-  if (p->batch > INT_MAX / p->levels || p->batch > 2147483647LL)
+  if (p->levels > 64) return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: levels must be <= 64");
+  if (p->batch > INT_MAX / p->levels)
     return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: batch * levels too large");
   if (!(p->confidence_threshold == p->confidence_threshold))
     return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: confidence_threshold is NaN");
@@ -519,7 +622,8 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
   else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, a.kk, rows, st);
   else rc = launch_stats_t<__half>(a, a.kk, rows, st);
   if (rc) return rc;
-  const size_t smem = static_cast<size_t>(a.cap) * (sizeof(double) + 2 * sizeof(int) + 2 * sizeof(float) + sizeof(int));
+  const size_t smem = static_cast<size_t>(a.cap) * (sizeof(double) + 2 * sizeof(int) + 2 * sizeof(float) + sizeof(int)) +
+                      static_cast<size_t>(a.levels) * (static_cast<size_t>(a.top_k) * 12 + 4);
   if (smem > 48 * 1024) {
     rc = check_cuda(cudaFuncSetAttribute(cand_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem)),
