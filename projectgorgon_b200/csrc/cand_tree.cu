@@ -4,17 +4,23 @@
 // synchronisation.  The reference runs both on the host: one softmax, one
 // entropy `.item()` and one top-k per head, then Python loops over the nodes.
 //
-// cand_stats_kernel — one CTA per (sequence, level) row of logits.  Pass 1
-//   reads the row from HBM (16-byte loads, 8 in flight per thread): every
-//   thread keeps an online (max m, Z = sum e^(x-m), T = sum e^(x-m) (x-m))
-//   and its own maximum; entropy = ln Z - T / Z.  A bound follows from the
-//   thread maxima: warp w's k-th largest leaves k logits at or above it, so
-//   the row's top k are all >= the largest such value.  Pass 2 re-reads the
-//   row (now in L2) and appends every logit at or above the bound to a
-//   shared-memory buffer, from which one warp picks the top k (descending;
+// cand_segment_kernel — one CTA per segment of a (sequence, level) row of
+//   logits: 256 threads x 8 vectors of 16 bytes, all copied at once into
+//   shared memory (cp.async).  Both passes then run as short loops over the
+//   thread's own vectors: a CTA executes its code once, so straight-line
+//   unrolled passes spent most of their time fetching instructions.  Pass 1:
+//   every thread's online
+//   (max m, Z = sum e^(x-m), T = sum e^(x-m) (x-m)) and its maximum.  A bound
+//   follows from the thread maxima (warp w's k-th largest leaves k logits at
+//   or above it, so the segment's top k are all >= the largest such value).
+//   Pass 2 appends every logit at or above the bound to a
+//   shared-memory buffer, from which one warp picks the segment's top k;
+//   segments with more ties at the bound than the buffer holds merge
+//   per-thread top-K lists instead.  Writes (m, Z, T) and the list.
+// cand_merge_kernel — one warp per row: merges the segments' statistics
+//   (entropy = ln Z - T / Z) and lists into the row's top k (descending;
 //   equal values by ascending id, a total order independent of the thread
-//   layout) and their softmax.  Rows with more ties at the bound than the
-//   buffer holds take a third pass with per-thread top-K lists instead.
+//   layout) and the softmax over them.
 // cand_tree_kernel — one warp per sequence.  The reference's expansion, level
 //   by level: a level's (parent, candidate) pairs are taken in the reference's
 //   order (parents sorted by their own logit, descending and stable, when a
@@ -34,14 +40,14 @@ namespace gorgon {
 constexpr uint32_t kErrCandCapacity = 1u << 3;
 
 namespace {
+using namespace sm100;
 
-// Threads per statistics CTA: fewer for the 32-entry lists, whose registers
-// would otherwise spill.
-template <int K>
-struct StatCfg {
-  static constexpr int kThreads = K <= 16 ? 512 : 256;
-  static constexpr int kWarps = kThreads / 32;
-};
+constexpr int kSegThreads = 256;                 // per segment CTA
+constexpr int kSegWarps = kSegThreads / 32;
+constexpr int kSegVecs = 8;                      // 16-byte vectors per thread
+constexpr int kSegBuf = 1024;                    // logits at or above the bound kept per segment
+template <typename T>
+constexpr int seg_elems() { return kSegThreads * kSegVecs * (16 / static_cast<int>(sizeof(T))); }
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct CandArgs {
@@ -52,6 +58,11 @@ struct CandArgs {
   double threshold;
   int use_path, entropy_weighted;
   int cap;
+  int segs;            // segments per row
+  float* part_m;       // [rows * segs][3]: m, Z, T of each segment
+  float* part_v;       // [rows * segs][K]: each segment's top K values ...
+  int32_t* part_i;     // ... and ids
+  int kmax;            // K, the list length of the launch
   int64_t* tokens;
   int32_t* parents;
   float* probs;
@@ -128,6 +139,14 @@ __device__ __forceinline__ void warp_merge(float (&kv)[K], int (&ki)[K]) {
   }
 }
 
+// 16-byte copy from global to shared memory that bypasses registers (and L1).
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sm100::smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
 // Online softmax statistics of one thread.
 struct Stats {
   float m = -INFINITY, z = 0.f, t = 0.f;
@@ -171,41 +190,26 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return r;
 }
 
-// Visits a row's logits as 16-byte vectors (8 in flight per thread), then the
-// scalar remainder, calling f(count tag, x[], first id) per vector or value.
-template <typename T, int NT, typename F>
-__device__ __forceinline__ void for_row(const T* src, int V, F&& f) {
+// The 16-byte vector of a row's logits that starts at element i0: one load
+// when the row is 16-byte aligned and the vector lies inside it, else
+// element by element with -inf past the end.
+template <typename T>
+__device__ __forceinline__ uint4 load_vec(const T* src, int i0, int V, bool aligned) {
   constexpr int kVec = 16 / sizeof(T);
-  constexpr int kUnroll = 8;
-  const bool vec = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
-  const int nvec = vec ? V / kVec : 0;
-  const uint4* src4 = reinterpret_cast<const uint4*>(src);
-  int v = threadIdx.x;
-  for (; v + (kUnroll - 1) * NT < nvec; v += kUnroll * NT) {
-    uint4 raw[kUnroll];
+  if (aligned && i0 + kVec <= V) return ld_stream(reinterpret_cast<const uint4*>(src + i0));
+  uint32_t w[4];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) raw[u] = ld_stream(src4 + v + u * NT);
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const T* e = reinterpret_cast<const T*>(&raw[u]);
-      float x[kVec];
-#pragma unroll
-      for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
-      f(std::integral_constant<int, kVec>(), x, (v + u * NT) * kVec);
+  for (int q = 0; q < 4; ++q) {
+    if constexpr (sizeof(T) == 4) {
+      w[q] = __float_as_uint(i0 + q < V ? Cvt<T>::to_f(src[i0 + q]) : -INFINITY);
+    } else {
+      const T lo = i0 + 2 * q < V ? src[i0 + 2 * q] : Cvt<T>::from_f(-INFINITY);
+      const T hi = i0 + 2 * q + 1 < V ? src[i0 + 2 * q + 1] : Cvt<T>::from_f(-INFINITY);
+      w[q] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+             (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
     }
   }
-  for (; v < nvec; v += NT) {
-    const uint4 raw = ld_stream(src4 + v);
-    const T* e = reinterpret_cast<const T*>(&raw);
-    float x[kVec];
-#pragma unroll
-    for (int j = 0; j < kVec; ++j) x[j] = Cvt<T>::to_f(e[j]);
-    f(std::integral_constant<int, kVec>(), x, v * kVec);
-  }
-  for (int i = nvec * kVec + threadIdx.x; i < V; i += NT) {
-    const float x = Cvt<T>::to_f(src[i]);
-    f(std::integral_constant<int, 1>(), &x, i);
-  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // k-th largest (1 <= k <= 32) of the warp's 32 values: bitonic sort across
@@ -225,38 +229,85 @@ __device__ __forceinline__ float warp_kth_largest(float x, int k) {
   return __shfl_sync(0xffffffffu, x, k - 1);
 }
 
-constexpr int kCandBuf = 2048;  // logits at or above the bound kept per row
-
 template <typename T, int K>
-__global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const CandArgs a) {
-  constexpr int NT = StatCfg<K>::kThreads;
-  constexpr int NW = StatCfg<K>::kWarps;
-  const int row = blockIdx.x;  // b * levels + l
+__global__ void __launch_bounds__(kSegThreads, K <= 16 ? 2 : 1) cand_segment_kernel(const CandArgs a) {
+  constexpr int kVec = 16 / sizeof(T);
+  const int S = a.segs;
+  const int row = blockIdx.x / S, seg = blockIdx.x - row * S;
   const int b = row / a.levels, l = row - b * a.levels;
   const T* src = static_cast<const T*>(a.logits) + static_cast<int64_t>(b) * a.lsb + static_cast<int64_t>(l) * a.lsl;
   const int V = a.vocab;
+  const int e0 = seg * seg_elems<T>();
+  const bool aligned = (reinterpret_cast<uintptr_t>(src) & 15u) == 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float s_m[NW], s_z[NW], s_t[NW], s_bound[NW];
-  __shared__ float s_kv[NW][K];
-  __shared__ int s_ki[NW][K];
-  __shared__ float s_bv[kCandBuf];
-  __shared__ int s_bi[kCandBuf];
+  __shared__ float s_m[kSegWarps], s_z[kSegWarps], s_t[kSegWarps], s_bound[kSegWarps];
+  __shared__ float s_kv[kSegWarps][K];
+  __shared__ int s_ki[kSegWarps][K];
+  __shared__ float s_bv[kSegBuf];
+  __shared__ int s_bi[kSegBuf];
   __shared__ int s_count;
   if (threadIdx.x == 0) s_count = 0;
 
-  // ---- pass 1 (HBM): online softmax statistics and this thread's maximum
+  // the whole segment in flight at once; vector u of this thread starts at
+  // element i0(u) and lands in s_seg[u][thread] (past the row's end: -inf)
+  __shared__ uint4 s_seg[kSegVecs][kSegThreads];
+  auto i0_of = [&](int u) { return e0 + (u * kSegThreads + static_cast<int>(threadIdx.x)) * kVec; };
+#pragma unroll
+  for (int u = 0; u < kSegVecs; ++u) {
+    const int i0 = i0_of(u);
+    if (aligned && i0 + kVec <= V) cp_async16(&s_seg[u][threadIdx.x], src + i0);
+    else s_seg[u][threadIdx.x] = load_vec<T>(src, i0, V, aligned);
+  }
+  cp_async_wait_all();  // each thread reads only its own vectors: no CTA barrier needed
+
+  // ---- pass 1: online softmax statistics (pairs in packed f32x2 arithmetic),
+  // each vector's maximum, and this thread's maximum
   Stats st;
-  float tmax = -INFINITY;
-  for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int) {
-    constexpr int N = decltype(n_tag)::value;
+  uint64_t z2 = 0, t2 = 0;  // (0.f, 0.f): the sums of the current base st.m
+  float vmax[kSegVecs];
+  const uint64_t l2e2 = f2_pack(kLog2e, kLog2e);
+#pragma unroll
+  for (int u = 0; u < kSegVecs; ++u) {
+    const uint4 raw = s_seg[u][threadIdx.x];
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float x[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) x[j] = fmaxf(Cvt<T>::to_f(e[j]), -1e30f);  // -inf adds nothing
     float cm = x[0];
 #pragma unroll
-    for (int j = 1; j < N; ++j) cm = fmaxf(cm, x[j]);
-    if (cm > st.m) st.rebase(cm);
+    for (int j = 1; j < kVec; j += 2) cm = fmax3(cm, x[j], j + 1 < kVec ? x[j + 1] : x[j]);
+    vmax[u] = cm;
+    if (cm > st.m) {  // new base: fold the packed sums in, rescale
+      float z0, z1, t0, t1;
+      f2_unpack(z2, z0, z1);
+      f2_unpack(t2, t0, t1);
+      st.z += z0 + z1;
+      st.t += t0 + t1;
+      st.rebase(cm);
+      z2 = t2 = 0;
+    }
+    const uint64_t nm2 = f2_pack(-st.m, -st.m);
 #pragma unroll
-    for (int j = 0; j < N; ++j) st.add(x[j]);
-    tmax = fmaxf(tmax, cm);
-  });
+    for (int j = 0; j < kVec; j += 2) {
+      const uint64_t d = f2_add(f2_pack(x[j], x[j + 1]), nm2);
+      float a0, a1;
+      f2_unpack(f2_mul(d, l2e2), a0, a1);
+      const uint64_t ee = f2_pack(ex2_approx(a0), ex2_approx(a1));
+      z2 = f2_add(z2, ee);
+      t2 = f2_fma(ee, d, t2);
+    }
+  }
+  {
+    float z0, z1, t0, t1;
+    f2_unpack(z2, z0, z1);
+    f2_unpack(t2, t0, t1);
+    st.z += z0 + z1;
+    st.t += t0 + t1;
+  }
+  float tmax = vmax[0];
+#pragma unroll
+  for (int u = 1; u < kSegVecs; ++u) tmax = fmaxf(tmax, vmax[u]);
+  if (tmax <= -1e30f) tmax = -INFINITY;  // nothing but padding
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     Stats other;
@@ -277,21 +328,29 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
   __syncthreads();
   float bound = s_bound[0];
 #pragma unroll
-  for (int w = 1; w < NW; ++w) bound = fmaxf(bound, s_bound[w]);
+  for (int w = 1; w < kSegWarps; ++w) bound = fmaxf(bound, s_bound[w]);
 
-  // ---- pass 2 (L2): every logit at or above the bound into the buffer
-  for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int id0) {
-    constexpr int N = decltype(n_tag)::value;
+  // ---- pass 2: the vectors whose maximum reaches the bound (rare) give their
+  // logits at or above it to the buffer, read back from shared memory
+  unsigned need = 0;
 #pragma unroll
-    for (int j = 0; j < N; ++j)
-      if (x[j] >= bound) {
+  for (int u = 0; u < kSegVecs; ++u) need |= (vmax[u] >= bound ? 1u : 0u) << u;
+  while (need) {
+    const int u = __ffs(need) - 1;
+    need &= need - 1;
+    const int i0 = i0_of(u);
+    const T* e = reinterpret_cast<const T*>(&s_seg[u][threadIdx.x]);
+    for (int j = 0; j < kVec; ++j) {
+      const float xv = Cvt<T>::to_f(e[j]);
+      if (xv >= bound && i0 + j < V) {
         const int slot = atomicAdd(&s_count, 1);
-        if (slot < kCandBuf) {
-          s_bv[slot] = x[j];
-          s_bi[slot] = id0 + j;
+        if (slot < kSegBuf) {
+          s_bv[slot] = xv;
+          s_bi[slot] = i0 + j;
         }
       }
-  });
+    }
+  }
   __syncthreads();
   const int count = s_count;
 
@@ -302,20 +361,23 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
     kv[j] = -INFINITY;
     ki[j] = -1;
   }
-  if (count <= kCandBuf) {
+  if (count <= kSegBuf) {
     if (warp == 0) {  // one warp picks the top K of the buffer
       for (int j = lane; j < count; j += 32) list_insert<K>(kv, ki, s_bv[j], s_bi[j]);
       warp_merge<K>(kv, ki);
     }
   } else {
-    // More ties at the bound than the buffer holds: exact per-thread lists
-    // over the row, filtered by the bound, merged per warp, then across warps.
-    for_row<T, NT>(src, V, [&](auto n_tag, const float* x, int id0) {
-      constexpr int N = decltype(n_tag)::value;
-#pragma unroll
-      for (int j = 0; j < N; ++j)
-        if (x[j] >= bound && (ki[K - 1] < 0 || x[j] > kv[K - 1])) list_insert<K>(kv, ki, x[j], id0 + j);
-    });
+    // More ties at the bound than the buffer holds: per-thread lists over the
+    // segment, merged per warp and then across warps.
+#pragma unroll 1
+    for (int u = 0; u < kSegVecs; ++u) {
+      const int i0 = i0_of(u);
+      const T* e = reinterpret_cast<const T*>(&s_seg[u][threadIdx.x]);
+      for (int j = 0; j < kVec; ++j) {
+        const float xv = Cvt<T>::to_f(e[j]);
+        if (xv >= bound && i0 + j < V && (ki[K - 1] < 0 || xv > kv[K - 1])) list_insert<K>(kv, ki, xv, i0 + j);
+      }
+    }
     warp_merge<K>(kv, ki);
     if (lane == 0) {
 #pragma unroll
@@ -328,16 +390,17 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
     if (warp == 0) {
 #pragma unroll
       for (int j = 0; j < K; ++j) {
-        kv[j] = lane < NW ? s_kv[lane][j] : -INFINITY;
-        ki[j] = lane < NW ? s_ki[lane][j] : -1;
+        kv[j] = lane < kSegWarps ? s_kv[lane][j] : -INFINITY;
+        ki[j] = lane < kSegWarps ? s_ki[lane][j] : -1;
       }
       warp_merge<K>(kv, ki);
     }
   }
   if (warp != 0) return;
 
+  // ---- this segment's statistics and list
   Stats all;
-  if (lane < NW) {
+  if (lane < kSegWarps) {
     all.m = s_m[lane];
     all.z = s_z[lane];
     all.t = s_t[lane];
@@ -350,6 +413,61 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
     other.t = __shfl_xor_sync(0xffffffffu, all.t, o);
     all.merge(other);
   }
+  const int64_t p = blockIdx.x;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const float v = __shfl_sync(0xffffffffu, kv[j], 0);
+    const int i = __shfl_sync(0xffffffffu, ki[j], 0);
+    if (lane == j) {
+      a.part_v[p * K + j] = v;
+      a.part_i[p * K + j] = i;
+    }
+  }
+  if (lane == 0) {
+    a.part_m[p * 3] = all.m;
+    a.part_m[p * 3 + 1] = all.z;
+    a.part_m[p * 3 + 2] = all.t;
+  }
+}
+
+// One warp: row `row`'s top k and entropy from its segments' lists and
+// (m, Z, T).  Writes them to the statistics outputs and returns this lane's
+// entry (lane j < kk: the j-th candidate's id, logit and probability).
+template <int K>
+__device__ __forceinline__ float merge_row(const CandArgs& a, int row, int& id_out, float& score_out,
+                                           float& prob_out) {
+  const int lane = threadIdx.x & 31;
+  const int S = a.segs;
+  const int64_t p0 = static_cast<int64_t>(row) * S;
+  Stats all;
+  for (int sg = lane; sg < S; sg += 32) {
+    Stats o;
+    o.m = a.part_m[(p0 + sg) * 3];
+    o.z = a.part_m[(p0 + sg) * 3 + 1];
+    o.t = a.part_m[(p0 + sg) * 3 + 2];
+    all.merge(o);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Stats other;
+    other.m = __shfl_xor_sync(0xffffffffu, all.m, o);
+    other.z = __shfl_xor_sync(0xffffffffu, all.z, o);
+    other.t = __shfl_xor_sync(0xffffffffu, all.t, o);
+    all.merge(other);
+  }
+  float kv[K];
+  int ki[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = -INFINITY;
+    ki[j] = -1;
+  }
+  const int n_entries = S * K;
+  for (int e = lane; e < n_entries; e += 32) {
+    const int id = a.part_i[p0 * K + e];
+    if (id >= 0) list_insert<K>(kv, ki, a.part_v[p0 * K + e], id);
+  }
+  warp_merge<K>(kv, ki);
   // lane 0 holds the top K; hand entry j to lane j
   float myv = -INFINITY;
   int myi = -1;
@@ -368,16 +486,17 @@ __global__ void __launch_bounds__(StatCfg<K>::kThreads) cand_stats_kernel(const 
   const float e = mine ? expf(myv - top) : 0.f;
   const float es = warp_sum(e);
   const int64_t o = static_cast<int64_t>(row) * a.top_k + lane;
-  if (mine) {
-    a.topk_ids[o] = myi;
-    a.topk_scores[o] = myv;
-    a.topk_probs[o] = e / es;
-  } else if (lane < a.top_k) {  // top_k above the vocabulary: empty slots
-    a.topk_ids[o] = -1;
-    a.topk_scores[o] = -INFINITY;
-    a.topk_probs[o] = 0.f;
+  id_out = mine ? myi : -1;
+  score_out = mine ? myv : -INFINITY;
+  prob_out = mine ? e / es : 0.f;
+  if (lane < a.top_k) {  // past min(top_k, vocab): empty slots
+    a.topk_ids[o] = id_out;
+    a.topk_scores[o] = score_out;
+    a.topk_probs[o] = prob_out;
   }
-  if (lane == 0) a.entropy[row] = all.z > 0.f ? logf(all.z) - all.t / all.z : 0.f;
+  const float ent = all.z > 0.f ? logf(all.z) - all.t / all.z : 0.f;
+  if (lane == 0) a.entropy[row] = ent;
+  return ent;
 }
 
 __device__ __forceinline__ unsigned lanes_below() {
@@ -390,6 +509,18 @@ __device__ __forceinline__ unsigned lanes_below() {
 // node, the current and next level's (node, logit) lists, the expansion order
 // of the current level, and the sequence's per-level statistics (read once,
 // coalesced, so the level loops wait on no global load).
+// One warp per row: the row's statistics from its segments (all rows at once,
+// rather than level after level inside the tree kernel, which measured 4x
+// slower).
+template <int K>
+__global__ void __launch_bounds__(256) cand_merge_kernel(const CandArgs a) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= a.batch * a.levels) return;
+  int id;
+  float sc, pr;
+  merge_row<K>(a, row, id, sc, pr);
+}
+
 __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int cap = a.cap;
@@ -413,7 +544,7 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
     for (int j = lane; j < a.levels; j += 32) s_ent[j] = a.entropy[static_cast<int64_t>(b) * a.levels + j];
     __syncwarp();
   }
-  const int K = a.kk;
+  const int kk = a.kk;
   const bool thr_on = a.threshold > 0.0;
   int64_t* tokens = a.tokens + static_cast<int64_t>(b) * cap;
   int32_t* parents = a.parents + static_cast<int64_t>(b) * cap;
@@ -452,9 +583,9 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   {
     const double thr = level_threshold(0);
     const int s0 = 0;
-    for (int base = 0; base < K && budget > 0; base += 32) {
+    for (int base = 0; base < kk && budget > 0; base += 32) {
       const int i = base + lane;
-      const bool valid = i < K;
+      const bool valid = i < kk;
       const float pr = valid ? s_prob[s0 + i] : 0.f;
       const bool pass = valid && !(thr_on && static_cast<double>(pr) < thr);
       const int n0 = n;
@@ -494,7 +625,7 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
     __syncwarp();
     const int nxt = cur ^ 1;
     int nxt_n = 0;
-    const int total = cur_n * K;
+    const int total = cur_n * kk;
     for (int base = 0; base < total && budget > 0; base += 32) {
       const int j = base + lane;
       const bool valid = j < total;
@@ -502,8 +633,8 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
       float pr = 0.f;
       double cp = 0.0;
       if (valid) {
-        const int pj = j / K;
-        i = j - pj * K;
+        const int pj = j / kk;
+        i = j - pj * kk;
         pnode = lvl_node[cur * cap + order[pj]];
         pr = s_prob[sl + i];
         cp = path[pnode] * static_cast<double>(pr);
@@ -540,13 +671,30 @@ __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
   }
 }
 
+template <typename T, int K>
+int launch_stats_k(const CandArgs& a, int rows, cudaStream_t st) {
+  cand_segment_kernel<T, K><<<static_cast<unsigned>(rows) * a.segs, kSegThreads, 0, st>>>(a);
+  return check_cuda(cudaGetLastError(), "candidate-tree segment launch");
+}
+
+template <int K>
+int launch_merge_k(const CandArgs& a, cudaStream_t st) {
+  cand_merge_kernel<K><<<static_cast<unsigned>((a.batch * a.levels + 7) / 8), 256, 0, st>>>(a);
+  return check_cuda(cudaGetLastError(), "candidate-tree merge launch");
+}
+
 template <typename T>
-int launch_stats_t(const CandArgs& a, int kmax, int rows, cudaStream_t st) {
-  if (kmax <= 4) cand_stats_kernel<T, 4><<<rows, StatCfg<4>::kThreads, 0, st>>>(a);
-  else if (kmax <= 8) cand_stats_kernel<T, 8><<<rows, StatCfg<8>::kThreads, 0, st>>>(a);
-  else if (kmax <= 16) cand_stats_kernel<T, 16><<<rows, StatCfg<16>::kThreads, 0, st>>>(a);
-  else cand_stats_kernel<T, 32><<<rows, StatCfg<32>::kThreads, 0, st>>>(a);
-  return check_cuda(cudaGetLastError(), "candidate-tree statistics launch");
+int launch_stats_t(const CandArgs& a, int rows, cudaStream_t st) {
+  if (a.kmax == 4) return launch_stats_k<T, 4>(a, rows, st);
+  if (a.kmax == 8) return launch_stats_k<T, 8>(a, rows, st);
+  if (a.kmax == 16) return launch_stats_k<T, 16>(a, rows, st);
+  return launch_stats_k<T, 32>(a, rows, st);
+}
+
+inline int list_len(int kk) { return kk <= 4 ? 4 : (kk <= 8 ? 8 : (kk <= 16 ? 16 : 32)); }
+inline int64_t segments(int dtype, int64_t vocab) {
+  const int64_t per = dtype == GORGON_F32 ? seg_elems<float>() : seg_elems<__nv_bfloat16>();
+  return (vocab + per - 1) / per;
 }
 
 constexpr size_t kWsAlign = 256;
@@ -555,12 +703,18 @@ inline size_t ws_align(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAli
 }  // namespace
 }  // namespace gorgon
 
+// Workspace: the per-row statistics (unless the caller takes them), then the
+// segments' (m, Z, T) and top-K lists.
 extern "C" size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tree_params* p) {
   using namespace gorgon;
-  if (!p || p->batch <= 0 || p->levels <= 0 || p->top_k <= 0) return 0;
+  if (!p || p->batch <= 0 || p->levels <= 0 || p->top_k <= 0 || p->vocab <= 0 || !dtype_ok(p->dtype)) return 0;
   const size_t rows = static_cast<size_t>(p->batch) * static_cast<size_t>(p->levels);
   const size_t per = rows * static_cast<size_t>(p->top_k);
-  return ws_align(per * sizeof(int32_t)) + 2 * ws_align(per * sizeof(float)) + ws_align(rows * sizeof(float));
+  const size_t parts = rows * static_cast<size_t>(segments(p->dtype, p->vocab));
+  const size_t K = static_cast<size_t>(list_len(static_cast<int>(p->vocab < p->top_k ? p->vocab : p->top_k)));
+  return ws_align(per * sizeof(int32_t)) + 2 * ws_align(per * sizeof(float)) + ws_align(rows * sizeof(float)) +
+         ws_align(parts * 3 * sizeof(float)) + ws_align(parts * K * sizeof(float)) +
+         ws_align(parts * K * sizeof(int32_t));
 }
 
 extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace, size_t workspace_bytes,
@@ -585,9 +739,10 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
     return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: confidence_threshold is NaN");
   if (!p->logits || !p->tokens || !p->parents || !p->probs || !p->n_nodes)
     return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: null pointer");
+  if (segments(p->dtype, p->vocab) * p->batch * p->levels > INT_MAX)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: batch * levels * vocab too large");
   const size_t need = gorgon_candidate_tree_workspace_size(p);
-  const bool all_stats = p->topk_ids && p->topk_scores && p->topk_probs && p->entropy;
-  if (!all_stats && (!workspace || workspace_bytes < need))
+  if (!workspace || workspace_bytes < need)
     return set_error(GORGON_ERR_WORKSPACE, "gorgon_candidate_tree: workspace too small");
   const int rows = static_cast<int>(p->batch * p->levels);
   const size_t per = static_cast<size_t>(rows) * static_cast<size_t>(p->top_k);
@@ -615,15 +770,30 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
   a.topk_probs = p->topk_probs ? p->topk_probs : reinterpret_cast<float*>(ws + ws_align(per * 4) + ws_align(per * 4));
   a.entropy = p->entropy ? p->entropy
                          : reinterpret_cast<float*>(ws + ws_align(per * 4) + 2 * ws_align(per * 4));
+  a.segs = static_cast<int>(segments(p->dtype, p->vocab));
+  a.kmax = list_len(a.kk);
+  {
+    const size_t parts = static_cast<size_t>(rows) * a.segs;
+    char* q = ws + 3 * ws_align(per * 4) + ws_align(static_cast<size_t>(rows) * 4);
+    a.part_m = reinterpret_cast<float*>(q);
+    q += ws_align(parts * 3 * sizeof(float));
+    a.part_v = reinterpret_cast<float*>(q);
+    q += ws_align(parts * a.kmax * sizeof(float));
+    a.part_i = reinterpret_cast<int32_t*>(q);
+  }
   a.err = device_error_word();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
-  if (p->dtype == GORGON_F32) rc = launch_stats_t<float>(a, a.kk, rows, st);
-  else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, a.kk, rows, st);
-  else rc = launch_stats_t<__half>(a, a.kk, rows, st);
+  if (p->dtype == GORGON_F32) rc = launch_stats_t<float>(a, rows, st);
+  else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, rows, st);
+  else rc = launch_stats_t<__half>(a, rows, st);
   if (rc) return rc;
   const size_t smem = static_cast<size_t>(a.cap) * (sizeof(double) + 2 * sizeof(int) + 2 * sizeof(float) + sizeof(int)) +
                       static_cast<size_t>(a.levels) * (static_cast<size_t>(a.top_k) * 12 + 4);
+  rc = a.kmax == 4 ? launch_merge_k<4>(a, st)
+                    : a.kmax == 8 ? launch_merge_k<8>(a, st)
+                                  : a.kmax == 16 ? launch_merge_k<16>(a, st) : launch_merge_k<32>(a, st);
+  if (rc) return rc;
   if (smem > 48 * 1024) {
     rc = check_cuda(cudaFuncSetAttribute(cand_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem)),

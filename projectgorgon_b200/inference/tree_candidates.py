@@ -110,7 +110,7 @@ def _run(lg: torch.Tensor, top_k: int, max_candidates: Optional[int], confidence
         p.topk_probs, p.entropy = stats.probs.data_ptr(), stats.entropy.data_ptr()
     lib = _abi.lib()
     with on_device(dev):
-        nbytes = lib.gorgon_candidate_tree_workspace_size(p) if stats is None else 0
+        nbytes = lib.gorgon_candidate_tree_workspace_size(p)
         ws = workspace(nbytes, dev)
         _abi.check(lib.gorgon_candidate_tree(p, ws.data_ptr(), ws.numel(), stream_ptr(dev)),
                    "gorgon_candidate_tree")
