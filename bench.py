@@ -51,6 +51,8 @@ NCU_TRAFFIC_BYTES = {
     # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
     # 0 written) scaled by 8 to 32 layers
     ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11108352,
+    # profiles/cand_segment_kernel_candidates-b32-h4-v128256.md: 32.893 MB read, 0 written
+    ("candidates-b32-h4-v128256", "cand_segment_kernel"): 32893440,
     # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 2181.164 MB read + 7.039 MB written
     ("wide-b8-p32k-n256", "tcgen05"): 2188202976,
 }
@@ -462,7 +464,7 @@ class CandidateWorkload:
         return G.build_candidate_trees(self.logits, top_k=c["top_k"], max_candidates=c["max_candidates"])
 
     def plan(self):
-        return {"backend": "cand_stats_kernel", "splits": None, "launches": 2}
+        return {"backend": "cand_segment_kernel", "splits": None, "launches": 3}
 
     def config(self, world: int, plan: dict) -> dict:
         c = self.cfg
