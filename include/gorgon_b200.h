@@ -258,8 +258,10 @@ GORGON_API int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream);
  * [batch]; slots from n_nodes[b] on hold -1 / -1 / 0.  A tree that would
  * outgrow max_nodes is cut there and sets device error bit 3.  topk_ids
  * int32, topk_scores and topk_probs float [batch, levels, top_k] and entropy
- * float [batch, levels] receive the per-row statistics when all four are
- * non-NULL (the workspace holds them otherwise).  The entropy is
+ * float [batch, levels] receive the per-row statistics when non-NULL (the
+ * workspace holds them otherwise).  The workspace of
+ * gorgon_candidate_tree_workspace_size() bytes is always required: it also
+ * holds every vocabulary segment's partial results.  The entropy is
  * ln Z - sum(e^x (x - max)) / Z, the reference's -sum p log(p + 1e-10)
  * without the 1e-10 (at most ~1e-5 apart for a 128k vocabulary).
  * top_k <= 32, levels <= 64, max_nodes <= 4096.
