@@ -204,6 +204,84 @@ class Workload:
         return cpu_baseline(self, budget_s=budget_s)
 
 
+class HeadShardWorkload(Workload):
+    """One layer split by kv head over the ranks (``--shard heads``, strong
+    scaling): rank r keeps the K/V cache of its Hkv / world kv heads and the
+    query heads that read them, computes their outputs, and an NCCL
+    all-gather assembles the layer's output [B, Hq, N, D] on every rank.  A
+    step is the local attention plus the gather; the attention alone is timed
+    beside it (``kernel_only_us``).  Trees and prefixes come from the
+    per-sequence seeds, each head's Q, K and V from a (sequence, head) seed,
+    so the job is the same for every number of ranks."""
+
+    scaling = "strong"
+
+    def __init__(self, name: str, dev: torch.device, rank: int, world: int):
+        cfg = WORKLOADS[name]
+        if isinstance(cfg["P"], tuple):
+            raise SystemExit("--shard heads needs a workload with one prefix length")
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, Hq, Hkv, D, N, P = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"], cfg["P"]
+        (h0, h1), (q0, q1) = sharding.shard_heads(Hkv, Hq, world, rank)
+        self.world, self.ragged, self.cu = world, False, None
+        rngs = [random.Random(1_000_003 + j) for j in range(B)]
+        self.prefixes = [P] * B
+        self.parents = [make_tree(cfg, r) for r in rngs]
+        self.max_depth = cfg["max_depth"]
+        dt = TORCH_DT[cfg["dtype"]]
+        self.dtype = dt
+        s = 1.0 / math.sqrt(D)
+        L = P + N
+        self.max_seqlen = L
+        self.q = torch.empty(B, q1 - q0, N, D, device=dev, dtype=dt)
+        self.k = torch.empty(B, h1 - h0, L, D, device=dev, dtype=dt)
+        self.v = torch.empty(B, h1 - h0, L, D, device=dev, dtype=dt)
+        for j in range(B):
+            for qh in range(q0, q1):
+                g = torch.Generator(device=dev).manual_seed(5_000_000 + j * Hq + qh)
+                self.q[j, qh - q0] = (torch.randn(N, D, device=dev, generator=g) * s).to(dt)
+            for h in range(h0, h1):
+                g = torch.Generator(device=dev).manual_seed(6_000_000 + j * Hkv + h)
+                self.k[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
+                self.v[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
+        self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
+        self.out = torch.empty(B, Hq, N, D, device=dev, dtype=dt)
+        esz = torch.tensor([], dtype=dt).element_size()
+        # this rank's share: its K/V, Q and output slice, and the parents
+        self.bytes = 2 * B * (h1 - h0) * L * D * esz + 2 * B * (q1 - q0) * N * D * esz + B * N * 4
+        self.flops = 4 * (q1 - q0) * N * D * B * L
+        self.tokens = B * N
+        self.kernel_events = []
+
+    def step(self):
+        st = torch.cuda.current_stream(self.dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        o = G.fused_tree_verify(self.q, self.k, self.v, **self.kwargs())
+        e1.record(st)
+        self.kernel_events.append((e0, e1))
+        return sharding.gather_heads(o, self.out)
+
+    def post(self, o):
+        """The output gather of one e2e step (a fresh buffer per step)."""
+        return sharding.gather_heads(o)
+
+    def config(self, world: int, plan: dict) -> dict:
+        c = super().config(world, plan)
+        c["parallelism"] = f"kv-head-sharded x{world}, NCCL all-gather of the output" if world > 1 else "single GPU"
+        c["batch"] = c.pop("batch_per_gpu")
+        c["shard"] = "heads"
+        return c
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        ev = self.kernel_events[-min(len(self.kernel_events), 50):]
+        torch.cuda.synchronize(self.dev)
+        k_ms = float(np.mean([a.elapsed_time(b) for a, b in ev])) if ev else float("nan")
+        return {"us_per_layer": round(ms_step * 1e3, 2), "kernel_only_us": round(k_ms * 1e3, 2),
+                "allgather_us": round((ms_step - k_ms) * 1e3, 2),
+                "tokens_verified_per_s": round(self.tokens / (ms_step * 1e-3), 1)}
+
+
 def _fill_normal(t: torch.Tensor, gen: torch.Generator, std: float) -> None:
     """Fills a bf16/fp32 tensor with N(0, std) in 64 MB fp32 pieces."""
     flat = t.view(-1)
@@ -737,7 +815,9 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     bufs = [(torch.empty_like(wl.q), torch.empty(kt_h.shape, dtype=kt_h.dtype, device=dev),
              torch.empty(vt_h.shape, dtype=vt_h.dtype, device=dev), torch.empty_like(wl.par_t))
             for _ in range(nbuf)]
-    outs_h = [torch.empty(wl.q.shape, dtype=wl.q.dtype).pin_memory() for _ in range(nbuf)]
+    post = getattr(wl, "post", None)
+    out_shape = wl.out.shape if post is not None else wl.q.shape
+    outs_h = [torch.empty(out_shape, dtype=wl.q.dtype).pin_memory() for _ in range(nbuf)]
     h2d = sum(t.numel() * t.element_size() for t in (q_h, kt_h, vt_h, par_h))
     d2h = outs_h[0].numel() * outs_h[0].element_size()
     s_c = torch.cuda.current_stream(dev)
@@ -775,6 +855,8 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
             wl.k[:, :, P:P + N].copy_(kt_d)
             wl.v[:, :, P:P + N].copy_(vt_d)
         o = G.fused_tree_verify(q_d, wl.k, wl.v, **dict(kw, parents=par_d))
+        if post is not None:
+            o = post(o)
         in_free[k].record(s_c)
         done[k].record(s_c)
         with torch.cuda.stream(s_out):
@@ -846,7 +928,12 @@ def run_ours(args):
     sharding.init(sharding.dist_env(), "nccl", dev, timeout_s=120)
     G.load_library()
     # weak scaling by sequence: rank r verifies global sequences [r*B, (r+1)*B)
-    wl = make_workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
+    if args.shard == "heads":
+        if WORKLOADS[args.workload].get("kind", "attn") != "attn":
+            raise SystemExit("--shard heads applies to the attention workloads")
+        wl = HeadShardWorkload(args.workload, dev, rank, world)
+    else:
+        wl = make_workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
     plan = wl.plan()
     total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
     total_ms = max_over_ranks(total_ms, world, dev)
@@ -889,7 +976,7 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 5),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": getattr(wl, "scaling", "weak"),
         "vs_baseline": None,
         "dtype": wl.cfg["dtype"],
         "data": wl.data,
@@ -1040,6 +1127,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=0, help="steps of the e2e loop (default: --steps)")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"],
+                    help="multi-GPU split: whole sequences per rank (weak scaling, default) or one layer's "
+                         "kv heads per rank with an NCCL all-gather of the output (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()

@@ -1,11 +1,19 @@
 """Spreading tree verification over the GPUs of one node.
 
-The verify path shards without any data exchange: sequences are independent
-(each has its own prefix cache, tree and logits), so every rank verifies its
-own contiguous run of sequences and nothing crosses NVLink on the data path.
-One process drives one GPU; ``torch.distributed`` (NCCL on GPUs, gloo on CPU)
-is only used for barriers, the max-over-ranks timing and, where a caller
-wants every rank to hold every sequence's output, :func:`gather_batch`.
+Two ways to split the work, one process per GPU:
+
+* by sequence (:func:`shard_range`, :func:`shard_by_weight`): sequences are
+  independent (each has its own prefix cache, tree and logits), so every rank
+  verifies its own contiguous run of sequences and nothing crosses NVLink on
+  the data path; :func:`gather_batch` is there for callers that want every
+  rank to hold every output;
+* by kv head (:func:`shard_heads`), for one layer that should finish sooner
+  on several GPUs: rank r keeps the key/value cache of its kv heads (and the
+  query heads that read them), computes their outputs, and
+  :func:`gather_heads` all-gathers the head slices into the layer's output.
+
+``torch.distributed`` (NCCL on GPUs, gloo on CPU) carries barriers, the
+max-over-ranks timing and the gathers.
 """
 from __future__ import annotations
 
@@ -17,8 +25,8 @@ from typing import List, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
-__all__ = ["DistEnv", "dist_env", "init", "shard_range", "shard_by_weight", "max_over_ranks",
-           "gather_batch"]
+__all__ = ["DistEnv", "dist_env", "init", "shard_range", "shard_by_weight", "shard_heads", "max_over_ranks",
+           "gather_batch", "gather_heads"]
 
 
 @dataclass(frozen=True)
@@ -72,6 +80,40 @@ def shard_by_weight(weights: Sequence[int], world: int, rank: int) -> Tuple[int,
         bounds.append(len(weights))
     bounds.append(len(weights))
     return bounds[rank], bounds[rank + 1]
+
+
+def shard_heads(heads_kv: int, heads_q: int, world: int, rank: int) -> Tuple[Tuple[int, int], Tuple[int, int]]:
+    """This rank's kv heads [h0, h1) and the query heads that read them,
+    [h0 * g, h1 * g) with g = heads_q / heads_kv.  Every rank gets the same
+    number of heads, so the output gather moves equal slices."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world of {world}")
+    if heads_kv % world or heads_q % heads_kv:
+        raise ValueError(f"{heads_kv} kv heads ({heads_q} query heads) do not split evenly over {world} ranks")
+    per = heads_kv // world
+    g = heads_q // heads_kv
+    return (rank * per, (rank + 1) * per), (rank * per * g, (rank + 1) * per * g)
+
+
+def gather_heads(local: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """All-gathers every rank's head slice [B, h, ...] into [B, world * h, ...]
+    (rank r's slice at heads r*h .. r*h + h): one all-gather of the equally
+    sized slices, then one copy into the batch-major layout.  With one rank
+    the slice is the whole output and is returned as it is."""
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return local
+    world = dist.get_world_size()
+    B, h = local.shape[0], local.shape[1]
+    rest = tuple(local.shape[2:])
+    flat = torch.empty((world,) + tuple(local.shape), dtype=local.dtype, device=local.device)
+    if dist.get_backend() == "nccl":
+        dist.all_gather_into_tensor(flat.view(-1), local.contiguous().view(-1))
+    else:
+        dist.all_gather(list(flat.unbind(0)), local.contiguous())
+    if out is None:
+        out = torch.empty((B, world * h) + rest, dtype=local.dtype, device=local.device)
+    out.view((B, world, h) + rest).copy_(flat.movedim(0, 1))
+    return out
 
 
 def max_over_ranks(value: float, device: torch.device = None) -> float:

@@ -1,5 +1,6 @@
 """Multi-rank host logic of the verify path, run as two gloo ranks on CPU:
-sequence sharding, the slowest-rank timing reduction and the output gather."""
+sequence and kv-head sharding, the slowest-rank timing reduction and the
+output gathers."""
 from __future__ import annotations
 
 import os
@@ -39,6 +40,16 @@ def test_shard_rejects_bad_rank():
         sharding.shard_range(4, 2, 2)
 
 
+def test_shard_heads_keeps_gqa_groups_together():
+    for world in (1, 2, 4, 8):
+        spans = [sharding.shard_heads(8, 32, world, r) for r in range(world)]
+        assert spans[0][0][0] == 0 and spans[-1][0][1] == 8 and spans[-1][1][1] == 32
+        for (h0, h1), (q0, q1) in spans:
+            assert q0 == 4 * h0 and q1 == 4 * h1 and h1 - h0 == 8 // world
+    with pytest.raises(ValueError):
+        sharding.shard_heads(8, 32, 3, 0)
+
+
 def _free_port() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -60,9 +71,13 @@ def _rank_main(rank, world, port, q):
         a, b = sharding.shard_range(B, world, rank)
         full = torch.arange(B * 4, dtype=torch.float32).view(B, 4)
         gathered = sharding.gather_batch(full[a:b].clone())
+        # each rank holds the outputs of its query heads; the gather restores [B, Hq, N, D]
+        o = torch.arange(3 * 8 * 5 * 2, dtype=torch.float32).view(3, 8, 5, 2)
+        _, (q0, q1) = sharding.shard_heads(4, 8, world, rank)
+        heads = sharding.gather_heads(o[:, q0:q1].clone())
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-        q.put((rank, t, bool(torch.equal(gathered, full))))
+        q.put((rank, t, bool(torch.equal(gathered, full)) and bool(torch.equal(heads, o))))
     except Exception as exc:  # pragma: no cover - reported to the parent
         q.put((rank, None, repr(exc)))
 
