@@ -44,8 +44,8 @@ from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tre
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
 NCU_TRAFFIC_BYTES = {
-    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.585 MB read + 3.880 MB written
-    ("verify-b16-p8192-n64", "tcgen05"): 553465600,
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.588 MB read + 5.126 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 554714112,
     # profiles/verify_kernel_verifier-b32-n64-v128256.md: 572.339 MB read + 3.123 MB written
     ("verifier-b32-n64-v128256", "verify_kernel"): 575461632,
     # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
