@@ -165,3 +165,22 @@ def test_tc_explicit_grid_sizes(grid):
     assert G.tree_attention_plan(q, k, v, parents=pars, backend="tcgen05", num_splits=grid)["splits"] == grid
     b = G.fused_tree_verify(q, k, v, pars, max_depth=5, backend="simt")
     torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
+
+
+@pytest.mark.parametrize("grid,out_dtype", [(100, None), (148, torch.float32)])
+def test_tc_many_pieces_per_unit(grid, out_dtype):
+    """Grids far above the unit count cut every unit into many pieces (up to
+    ten per unit here, odd and even counts): the last piece to finish a warp's
+    rows merges them all, output and log-sum-exp, in any output dtype."""
+    B, N, P = 1, 64, 2048
+    pars = torch.tensor(_trees(B, N, seed=grid), device="cuda")
+    q, k, v = _inputs(B, 32, 8, N, P + N, seed=grid)
+    plan = G.tree_attention_plan(q, k, v, parents=pars, backend="tcgen05", num_splits=grid, out_dtype=out_dtype)
+    assert plan["splits"] == grid and plan["launches"] == 2
+    a, la = G.tree_attention(q, k, v, parents=pars, max_depth=5, backend="tcgen05", num_splits=grid,
+                             out_dtype=out_dtype, return_lse=True)
+    b, lb = G.tree_attention(q, k, v, parents=pars, max_depth=5, backend="simt", out_dtype=out_dtype,
+                             return_lse=True)
+    assert a.dtype == b.dtype
+    torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
+    torch.testing.assert_close(la, lb, atol=1e-3, rtol=1e-4)
