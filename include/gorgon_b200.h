@@ -289,6 +289,40 @@ GORGON_API size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tr
 GORGON_API int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace,
                                      size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Candidate trees straight from the Medusa heads' last Linear.  Replaces
+ * MedusaHead.forward's lm_head (src/gorgon/models/medusa_heads.py:42-47)
+ * followed by _topk_per_head (src/gorgon/inference/tree_candidates.py:42-81)
+ * and the expansion of build_candidate_tree (:92-245): the outputs and rules
+ * are gorgon_candidate_tree's, with
+ *   logits[b, l, v] = sum_i hidden[b, l, i] * lm_head[l][v, i]
+ * accumulated in fp32 and rounded to tree.dtype (the dtype the Linear would
+ * return) inside the kernel; the logits are never written to memory, and
+ * tree.logits and its strides are ignored.  A logit may differ from a
+ * library GEMM's by one rounding step of tree.dtype (summation order).
+ *
+ * hidden [batch, levels, hidden_size]: the input of head l's lm_head (after
+ * its norm and residual blocks) for sequence b.  lm_head: a HOST array of
+ * `levels` device pointers, head l's weight [vocab, hidden_size] with rows
+ * lm_head_stride_v elements apart.  hidden and the weights are x_dtype
+ * (GORGON_BF16 or GORGON_F16), 16-byte aligned, with hidden_size and every
+ * stride a multiple of 8.  batch <= 4 (above that the dot products outrun
+ * the CUDA cores: use a GEMM and gorgon_candidate_tree), hidden_size <= 8192,
+ * levels <= 64.  The workspace of gorgon_head_candidate_tree_workspace_size()
+ * bytes is always required.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+  gorgon_candidate_tree_params tree;
+  int32_t x_dtype;
+  const void* hidden; int64_t hidden_stride_b, hidden_stride_l;
+  int64_t hidden_size;
+  const void* const* lm_head; int64_t lm_head_stride_v;
+} gorgon_head_candidate_params;
+
+GORGON_API size_t gorgon_head_candidate_tree_workspace_size(const gorgon_head_candidate_params* p);
+GORGON_API int gorgon_head_candidate_tree(const gorgon_head_candidate_params* p, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

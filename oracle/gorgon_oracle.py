@@ -329,6 +329,28 @@ def head_topk(logits: np.ndarray, k: int) -> Tuple[np.ndarray, np.ndarray, np.nd
     return order.astype(np.int64), scores, probs, entropy
 
 
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bfloat16 (ties to even), returned as float32."""
+    u = np.asarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
+def head_logits(hidden: np.ndarray, lm_heads: Sequence[np.ndarray], round_to: Optional[str] = None) -> np.ndarray:
+    """Logits of every Medusa head's last layer for one sequence
+    (``MedusaHead.forward``, ``src/gorgon/models/medusa_heads.py:42-47``: a
+    bias-free ``nn.Linear``): ``logits[l, v] = sum_i hidden[l, i] * W_l[v, i]``
+    in float64, then as the Linear's output dtype: ``round_to`` "bf16", "f16"
+    or None (float32).  ``hidden [L, H]`` holds head ``l``'s Linear input."""
+    h = np.asarray(hidden, dtype=np.float64)
+    out = np.stack([np.asarray(w, dtype=np.float64) @ h[l] for l, w in enumerate(lm_heads)]).astype(np.float32)
+    if round_to == "bf16":
+        return round_bf16(out)
+    if round_to == "f16":
+        return out.astype(np.float16).astype(np.float32)
+    return out
+
+
 def build_candidate_tree(levels, top_k: int, max_candidates: Optional[int] = None,
                          confidence_threshold: float = 0.0, use_path_confidence: bool = False,
                          entropy_weighted: bool = False) -> Tuple[List[int], List[int], List[float]]:

@@ -94,6 +94,16 @@ class CandidateTreeParams(Structure):
     ]
 
 
+class HeadCandidateParams(Structure):
+    _fields_ = [
+        ("tree", CandidateTreeParams),
+        ("x_dtype", c_int32),
+        ("hidden", c_void_p), ("hidden_stride_b", c_int64), ("hidden_stride_l", c_int64),
+        ("hidden_size", c_int64),
+        ("lm_head", c_void_p), ("lm_head_stride_v", c_int64),
+    ]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "gorgon_abi_version": (c_int, []),
@@ -110,6 +120,8 @@ SIGNATURES = {
     "gorgon_kv_trim": (c_int, [POINTER(KvTrimParams), c_void_p]),
     "gorgon_candidate_tree_workspace_size": (c_size_t, [POINTER(CandidateTreeParams)]),
     "gorgon_candidate_tree": (c_int, [POINTER(CandidateTreeParams), c_void_p, c_size_t, c_void_p]),
+    "gorgon_head_candidate_tree_workspace_size": (c_size_t, [POINTER(HeadCandidateParams)]),
+    "gorgon_head_candidate_tree": (c_int, [POINTER(HeadCandidateParams), c_void_p, c_size_t, c_void_p]),
 }
 
 _lib = None

@@ -28,8 +28,12 @@
 //   its pair against the thresholds, a ballot gives every passing pair its
 //   rank, and pairs are kept while the budget lasts.  Path probabilities and
 //   thresholds are in double precision, as the reference's Python floats.
+// head_segment_kernel — the heads' last Linear fused with the segment
+//   statistics (gorgon_head_candidate_tree): the logits are computed from the
+//   lm_head inputs and weights in the kernel and never stored.
 #include <climits>
 #include <cmath>
+#include <cstdio>
 #include <type_traits>
 
 #include "common.cuh"
@@ -430,23 +434,61 @@ __global__ void __launch_bounds__(kSegThreads, K <= 16 ? 2 : 1) cand_segment_ker
   }
 }
 
-// One warp: row `row`'s top k and entropy from its segments' lists and
-// (m, Z, T).  Writes them to the statistics outputs and returns this lane's
-// entry (lane j < kk: the j-th candidate's id, logit and probability).
+// Per lane: statistics and a top-K list over segments [s0, s1) of the row
+// whose partials start at p0.  Loads go out in batches (4 segments'
+// statistics, then 8 list entries per lane) before any is used: with
+// hundreds of segments per row (the fused heads) a load per loop trip would
+// leave the warp waiting on memory each time.
 template <int K>
-__device__ __forceinline__ float merge_row(const CandArgs& a, int row, int& id_out, float& score_out,
-                                           float& prob_out) {
+__device__ __forceinline__ void scan_segments(const CandArgs& a, int64_t p0, int s0, int s1, Stats& all,
+                                              float (&kv)[K], int (&ki)[K]) {
   const int lane = threadIdx.x & 31;
-  const int S = a.segs;
-  const int64_t p0 = static_cast<int64_t>(row) * S;
-  Stats all;
-  for (int sg = lane; sg < S; sg += 32) {
-    Stats o;
-    o.m = a.part_m[(p0 + sg) * 3];
-    o.z = a.part_m[(p0 + sg) * 3 + 1];
-    o.t = a.part_m[(p0 + sg) * 3 + 2];
-    all.merge(o);
+  for (int sg0 = s0; sg0 < s1; sg0 += 32 * 4) {
+    float m[4], z[4], t[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int sg = sg0 + u * 32 + lane;
+      const bool ok = sg < s1;
+      m[u] = ok ? a.part_m[(p0 + sg) * 3] : -INFINITY;
+      z[u] = ok ? a.part_m[(p0 + sg) * 3 + 1] : 0.f;
+      t[u] = ok ? a.part_m[(p0 + sg) * 3 + 2] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      Stats o;
+      o.m = m[u];
+      o.z = z[u];
+      o.t = t[u];
+      all.merge(o);
+    }
   }
+  const int e1 = s1 * K;
+  for (int e0 = s0 * K; e0 < e1; e0 += 32 * 8) {
+    float v[8];
+    int id[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * 32 + lane;
+      const bool ok = e < e1;
+      id[u] = ok ? a.part_i[p0 * K + e] : -1;
+      v[u] = ok ? a.part_v[p0 * K + e] : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (ahead(v[u], id[u], kv[K - 1], ki[K - 1])) list_insert<K>(kv, ki, v[u], id[u]);
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void empty_list(float (&kv)[K], int (&ki)[K]) {
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = -INFINITY;
+    ki[j] = -1;
+  }
+}
+
+__device__ __forceinline__ void warp_reduce_stats(Stats& all) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     Stats other;
@@ -455,18 +497,16 @@ __device__ __forceinline__ float merge_row(const CandArgs& a, int row, int& id_o
     other.t = __shfl_xor_sync(0xffffffffu, all.t, o);
     all.merge(other);
   }
-  float kv[K];
-  int ki[K];
-#pragma unroll
-  for (int j = 0; j < K; ++j) {
-    kv[j] = -INFINITY;
-    ki[j] = -1;
-  }
-  const int n_entries = S * K;
-  for (int e = lane; e < n_entries; e += 32) {
-    const int id = a.part_i[p0 * K + e];
-    if (id >= 0) list_insert<K>(kv, ki, a.part_v[p0 * K + e], id);
-  }
+}
+
+// One warp, from every lane's partial statistics and top-K list: row `row`'s
+// top k and entropy.  Writes them to the statistics outputs and returns this
+// lane's entry (lane j < kk: the j-th candidate's id, logit and probability).
+template <int K>
+__device__ __forceinline__ float finish_row(const CandArgs& a, int row, Stats all, float (&kv)[K], int (&ki)[K],
+                                            int& id_out, float& score_out, float& prob_out) {
+  const int lane = threadIdx.x & 31;
+  warp_reduce_stats(all);
   warp_merge<K>(kv, ki);
   // lane 0 holds the top K; hand entry j to lane j
   float myv = -INFINITY;
@@ -499,6 +539,18 @@ __device__ __forceinline__ float merge_row(const CandArgs& a, int row, int& id_o
   return ent;
 }
 
+// One warp: row `row`'s top k and entropy from all of its segments.
+template <int K>
+__device__ __forceinline__ float merge_row(const CandArgs& a, int row, int& id_out, float& score_out,
+                                           float& prob_out) {
+  Stats all;
+  float kv[K];
+  int ki[K];
+  empty_list<K>(kv, ki);
+  scan_segments<K>(a, static_cast<int64_t>(row) * a.segs, 0, a.segs, all, kv, ki);
+  return finish_row<K>(a, row, all, kv, ki, id_out, score_out, prob_out);
+}
+
 __device__ __forceinline__ unsigned lanes_below() {
   unsigned r;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(r));
@@ -519,6 +571,205 @@ __global__ void __launch_bounds__(256) cand_merge_kernel(const CandArgs a) {
   int id;
   float sc, pr;
   merge_row<K>(a, row, id, sc, pr);
+}
+
+// Rows with many segments (the fused heads: hundreds): one CTA per row, each
+// of its 8 warps scans an eighth of the segments, warp 0 merges the eight
+// results through shared memory.
+constexpr int kWideMergeSegs = 64;  // segments per row above which the wide merge runs
+
+template <int K>
+__global__ void __launch_bounds__(256) cand_merge_wide_kernel(const CandArgs a) {
+  __shared__ float s_m[8], s_z[8], s_t[8];
+  __shared__ float s_v[8][K];
+  __shared__ int s_i[8][K];
+  const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = a.segs;
+  const int per = (S + 7) / 8;
+  const int s0 = min(S, warp * per), s1 = min(S, s0 + per);
+  Stats st;
+  float kv[K];
+  int ki[K];
+  empty_list<K>(kv, ki);
+  scan_segments<K>(a, static_cast<int64_t>(row) * S, s0, s1, st, kv, ki);
+  warp_reduce_stats(st);
+  warp_merge<K>(kv, ki);
+  if (lane == 0) {
+    s_m[warp] = st.m;
+    s_z[warp] = st.z;
+    s_t[warp] = st.t;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      s_v[warp][j] = kv[j];
+      s_i[warp][j] = ki[j];
+    }
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  Stats all;
+  if (lane < 8) {
+    all.m = s_m[lane];
+    all.z = s_z[lane];
+    all.t = s_t[lane];
+  }
+  empty_list<K>(kv, ki);
+  for (int e = lane; e < 8 * K; e += 32) {
+    const int w = e / K, j = e - w * K;
+    if (ahead(s_v[w][j], s_i[w][j], kv[K - 1], ki[K - 1])) list_insert<K>(kv, ki, s_v[w][j], s_i[w][j]);
+  }
+  int id;
+  float sc, pr;
+  finish_row<K>(a, row, all, kv, ki, id, sc, pr);
+}
+
+// ------------------------------------------------------------ fused heads
+// head_segment_kernel — the last Linear of every Medusa head fused with the
+// segment statistics: CTA (segment s, level l) computes the logits of vocab
+// rows [R s, R s + R) of head l (R <= 256, chosen so that the launch is a
+// whole number of waves of resident CTAs) for every sequence of the batch
+// (at most 4) and leaves the same per-segment (m, Z, T) and top-K list as
+// cand_segment_kernel, so the merge and tree kernels run unchanged.  The
+// head inputs of level l (batch x hidden, 16-bit) sit in shared memory; each
+// warp takes one weight row at a time, a lane holding 16 of its 16-byte
+// vectors (the whole row of a 4096-wide head in flight per warp), and
+// accumulates the batch's dot products in packed fp32 pairs.  Each logit is
+// rounded to the head's output dtype before the statistics, as the logits of
+// the Linear would be.  The weights stream from HBM once per launch; the
+// logits never leave the SM.
+constexpr int kHeadThreads = 256;
+constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kHeadRows = 256;       // most vocab rows per segment
+constexpr int kHeadCtasPerSm = 2;    // resident segment CTAs per SM (the launch bounds)
+constexpr int kHeadChunk = 16;       // 16-byte weight vectors per lane in flight
+constexpr int kHeadMaxBatch = 4;
+constexpr int kHeadMaxLevels = 64;
+constexpr int kHeadMaxHidden = 8192;
+
+struct HeadArgs {
+  const void* x;  // [batch, levels, hidden]
+  int64_t xsb, xsl;
+  const void* w[kHeadMaxLevels];  // per level: [vocab, hidden], rows wsv elements apart
+  int64_t wsv;
+  int hidden;       // a multiple of 8
+  int seg_rows;     // vocab rows per segment (<= kHeadRows)
+  int logit_dtype;  // rounding of each logit
+};
+
+__device__ __forceinline__ float round_logit(float x, int dt) {
+  if (dt == GORGON_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  if (dt == GORGON_F16) return __half2float(__float2half_rn(x));
+  return x;
+}
+
+// Eight 16-bit values -> four packed fp32 pairs (element order kept).
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, uint64_t (&p)[4]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      p[k] = sm100::f2_pack(__uint_as_float(w[k] << 16), __uint_as_float(w[k] & 0xffff0000u));
+    } else {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      p[k] = sm100::f2_pack(f.x, f.y);
+    }
+  }
+}
+
+template <typename T, int NB, int K>
+__global__ void __launch_bounds__(kHeadThreads, kHeadCtasPerSm) head_segment_kernel(const CandArgs a, const HeadArgs h) {
+  extern __shared__ uint4 s_x[];  // [NB][hidden / 8]
+  __shared__ float s_lg[NB][kHeadRows];
+  const int S = a.segs;
+  const int seg = blockIdx.x, l = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H8 = h.hidden >> 3;
+  const int B = a.batch;
+  for (int i = threadIdx.x; i < NB * H8; i += kHeadThreads) {
+    const int b = i / H8, j = i - b * H8;
+    s_x[i] = b < B ? *reinterpret_cast<const uint4*>(static_cast<const T*>(h.x) + b * h.xsb + l * h.xsl + j * 8)
+                   : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const T* W = static_cast<const T*>(h.w[l]);
+  const int v0 = seg * h.seg_rows;
+  const int nrows = min(h.seg_rows, a.vocab - v0);
+  for (int r = warp; r < nrows; r += kHeadWarps) {
+    const uint4* wrow = reinterpret_cast<const uint4*>(W + static_cast<int64_t>(v0 + r) * h.wsv);
+    uint64_t acc[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = 0;  // (0.f, 0.f)
+    for (int j0 = 0; j0 < H8; j0 += 32 * kHeadChunk) {
+      uint4 wv[kHeadChunk];
+#pragma unroll
+      for (int u = 0; u < kHeadChunk; ++u) {
+        const int j = j0 + u * 32 + lane;
+        wv[u] = j < H8 ? ld_stream(wrow + j) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < kHeadChunk; ++u) {
+        const int j = j0 + u * 32 + lane;
+        if (j < H8) {
+          uint64_t wp[4];
+          unpack8<T>(wv[u], wp);
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            uint64_t xp[4];
+            unpack8<T>(s_x[b * H8 + j], xp);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) acc[b] = sm100::f2_fma(wp[k], xp[k], acc[b]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      float lo, hi;
+      sm100::f2_unpack(acc[b], lo, hi);
+      const float s = warp_sum(lo + hi);
+      if (lane == 0) s_lg[b][r] = round_logit(s, h.logit_dtype);
+    }
+  }
+  __syncthreads();
+  if (warp >= B) return;
+  // warp b: the segment's statistics and top K for sequence b
+  const int b = warp;
+  const float* lg = s_lg[b];
+  float mx = -INFINITY;
+  for (int i = lane; i < nrows; i += 32) mx = fmaxf(mx, lg[i]);
+  Stats st;
+  if (mx > -INFINITY) {
+    st.rebase(mx);
+    for (int i = lane; i < nrows; i += 32) st.add(lg[i]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Stats other;
+    other.m = __shfl_xor_sync(0xffffffffu, st.m, o);
+    other.z = __shfl_xor_sync(0xffffffffu, st.z, o);
+    other.t = __shfl_xor_sync(0xffffffffu, st.t, o);
+    st.merge(other);
+  }
+  float kv[K];
+  int ki[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    kv[j] = -INFINITY;
+    ki[j] = -1;
+  }
+  for (int i = lane; i < nrows; i += 32) list_insert<K>(kv, ki, lg[i], v0 + i);
+  warp_merge<K>(kv, ki);
+  if (lane == 0) {
+    const int64_t p = (static_cast<int64_t>(b) * a.levels + l) * S + seg;
+    a.part_m[p * 3] = st.m;
+    a.part_m[p * 3 + 1] = st.z;
+    a.part_m[p * 3 + 2] = st.t;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      a.part_v[p * K + j] = kv[j];
+      a.part_i[p * K + j] = ki[j];
+    }
+  }
 }
 
 __global__ void __launch_bounds__(32) cand_tree_kernel(const CandArgs a) {
@@ -679,7 +930,10 @@ int launch_stats_k(const CandArgs& a, int rows, cudaStream_t st) {
 
 template <int K>
 int launch_merge_k(const CandArgs& a, cudaStream_t st) {
-  cand_merge_kernel<K><<<static_cast<unsigned>((a.batch * a.levels + 7) / 8), 256, 0, st>>>(a);
+  if (a.segs > kWideMergeSegs)
+    cand_merge_wide_kernel<K><<<static_cast<unsigned>(a.batch * a.levels), 256, 0, st>>>(a);
+  else
+    cand_merge_kernel<K><<<static_cast<unsigned>((a.batch * a.levels + 7) / 8), 256, 0, st>>>(a);
   return check_cuda(cudaGetLastError(), "candidate-tree merge launch");
 }
 
@@ -700,53 +954,62 @@ inline int64_t segments(int dtype, int64_t vocab) {
 constexpr size_t kWsAlign = 256;
 inline size_t ws_align(size_t x) { return (x + kWsAlign - 1) / kWsAlign * kWsAlign; }
 
-}  // namespace
-}  // namespace gorgon
+// Segments per level of the fused heads: at least vocab / 256, rounded up so
+// that segments x levels fills whole waves of resident CTAs (a launch of 6.8
+// waves leaves most SMs idle for the last 0.8).
+inline int64_t head_seg_rows(int64_t vocab, int64_t levels) {
+  const int64_t slots = static_cast<int64_t>(sm_count()) * kHeadCtasPerSm;
+  const int64_t min_segs = (vocab + kHeadRows - 1) / kHeadRows;
+  const int64_t waves = (min_segs * levels + slots - 1) / slots;
+  const int64_t segs = (waves * slots + levels - 1) / levels;
+  const int64_t rows = (vocab + segs - 1) / segs;
+  return rows < 1 ? 1 : rows;
+}
+inline int64_t head_segments(int64_t vocab, int64_t levels) {
+  const int64_t rows = head_seg_rows(vocab, levels);
+  return (vocab + rows - 1) / rows;
+}
 
 // Workspace: the per-row statistics (unless the caller takes them), then the
 // segments' (m, Z, T) and top-K lists.
-extern "C" size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tree_params* p) {
-  using namespace gorgon;
-  if (!p || p->batch <= 0 || p->levels <= 0 || p->top_k <= 0 || p->vocab <= 0 || !dtype_ok(p->dtype)) return 0;
+size_t workspace_bytes(const gorgon_candidate_tree_params* p, int64_t segs) {
   const size_t rows = static_cast<size_t>(p->batch) * static_cast<size_t>(p->levels);
   const size_t per = rows * static_cast<size_t>(p->top_k);
-  const size_t parts = rows * static_cast<size_t>(segments(p->dtype, p->vocab));
+  const size_t parts = rows * static_cast<size_t>(segs);
   const size_t K = static_cast<size_t>(list_len(static_cast<int>(p->vocab < p->top_k ? p->vocab : p->top_k)));
   return ws_align(per * sizeof(int32_t)) + 2 * ws_align(per * sizeof(float)) + ws_align(rows * sizeof(float)) +
          ws_align(parts * 3 * sizeof(float)) + ws_align(parts * K * sizeof(float)) +
          ws_align(parts * K * sizeof(int32_t));
 }
 
-extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace, size_t workspace_bytes,
-                                     void* stream) {
-  using namespace gorgon;
-  if (!p) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: params is null");
-  if (!dtype_ok(p->dtype)) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: unknown dtype");
-  if (p->batch < 0 || p->levels < 0 || p->vocab < 0)
-    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: negative size");
-  if (p->batch == 0) return GORGON_OK;
-  if (p->levels < 1) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: levels must be >= 1");
-  if (p->vocab < 1 || p->vocab > INT_MAX - 16)
-    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: vocab outside [1, 2^31)");
-  if (p->top_k < 1 || p->top_k > 32)
-    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: top_k must be in [1, 32]");
-  if (p->max_nodes < 1 || p->max_nodes > 4096)
-    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: max_nodes must be in [1, 4096]");
-  if (p->levels > 64) return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: levels must be <= 64");
-  if (p->batch > INT_MAX / p->levels)
-    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: batch * levels too large");
+// Checks the tree parameters that both entry points share; 1 when there is
+// nothing to do (an empty batch), 0 to go on, else the error code.
+int check_tree(const gorgon_candidate_tree_params* p, int64_t segs, const char* who) {
+  char msg[160];
+  auto fail = [&](int code, const char* what) {
+    snprintf(msg, sizeof(msg), "%s: %s", who, what);
+    return set_error(code, msg);
+  };
+  if (!dtype_ok(p->dtype)) return fail(GORGON_ERR_INVALID, "unknown dtype");
+  if (p->batch < 0 || p->levels < 0 || p->vocab < 0) return fail(GORGON_ERR_INVALID, "negative size");
+  if (p->batch == 0) return 1;
+  if (p->levels < 1) return fail(GORGON_ERR_INVALID, "levels must be >= 1");
+  if (p->vocab < 1 || p->vocab > INT_MAX - 16) return fail(GORGON_ERR_INVALID, "vocab outside [1, 2^31)");
+  if (p->top_k < 1 || p->top_k > 32) return fail(GORGON_ERR_UNSUPPORTED, "top_k must be in [1, 32]");
+  if (p->max_nodes < 1 || p->max_nodes > 4096) return fail(GORGON_ERR_UNSUPPORTED, "max_nodes must be in [1, 4096]");
+  if (p->levels > 64) return fail(GORGON_ERR_UNSUPPORTED, "levels must be <= 64");
+  if (p->batch > INT_MAX / p->levels) return fail(GORGON_ERR_UNSUPPORTED, "batch * levels too large");
   if (!(p->confidence_threshold == p->confidence_threshold))
-    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: confidence_threshold is NaN");
-  if (!p->logits || !p->tokens || !p->parents || !p->probs || !p->n_nodes)
-    return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: null pointer");
-  if (segments(p->dtype, p->vocab) * p->batch * p->levels > INT_MAX)
-    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_candidate_tree: batch * levels * vocab too large");
-  const size_t need = gorgon_candidate_tree_workspace_size(p);
-  if (!workspace || workspace_bytes < need)
-    return set_error(GORGON_ERR_WORKSPACE, "gorgon_candidate_tree: workspace too small");
+    return fail(GORGON_ERR_INVALID, "confidence_threshold is NaN");
+  if (!p->tokens || !p->parents || !p->probs || !p->n_nodes) return fail(GORGON_ERR_INVALID, "null pointer");
+  if (segs * p->batch * p->levels > INT_MAX) return fail(GORGON_ERR_UNSUPPORTED, "batch * levels * vocab too large");
+  return 0;
+}
+
+// The kernels' arguments over a checked parameter block and its workspace.
+CandArgs make_args(const gorgon_candidate_tree_params* p, int64_t segs, char* ws) {
   const int rows = static_cast<int>(p->batch * p->levels);
   const size_t per = static_cast<size_t>(rows) * static_cast<size_t>(p->top_k);
-  char* ws = static_cast<char*>(workspace);
   CandArgs a{};
   a.logits = p->logits;
   a.lsb = p->logits_stride_b;
@@ -770,29 +1033,26 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
   a.topk_probs = p->topk_probs ? p->topk_probs : reinterpret_cast<float*>(ws + ws_align(per * 4) + ws_align(per * 4));
   a.entropy = p->entropy ? p->entropy
                          : reinterpret_cast<float*>(ws + ws_align(per * 4) + 2 * ws_align(per * 4));
-  a.segs = static_cast<int>(segments(p->dtype, p->vocab));
+  a.segs = static_cast<int>(segs);
   a.kmax = list_len(a.kk);
-  {
-    const size_t parts = static_cast<size_t>(rows) * a.segs;
-    char* q = ws + 3 * ws_align(per * 4) + ws_align(static_cast<size_t>(rows) * 4);
-    a.part_m = reinterpret_cast<float*>(q);
-    q += ws_align(parts * 3 * sizeof(float));
-    a.part_v = reinterpret_cast<float*>(q);
-    q += ws_align(parts * a.kmax * sizeof(float));
-    a.part_i = reinterpret_cast<int32_t*>(q);
-  }
+  const size_t parts = static_cast<size_t>(rows) * a.segs;
+  char* q = ws + 3 * ws_align(per * 4) + ws_align(static_cast<size_t>(rows) * 4);
+  a.part_m = reinterpret_cast<float*>(q);
+  q += ws_align(parts * 3 * sizeof(float));
+  a.part_v = reinterpret_cast<float*>(q);
+  q += ws_align(parts * a.kmax * sizeof(float));
+  a.part_i = reinterpret_cast<int32_t*>(q);
   a.err = device_error_word();
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (p->dtype == GORGON_F32) rc = launch_stats_t<float>(a, rows, st);
-  else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, rows, st);
-  else rc = launch_stats_t<__half>(a, rows, st);
-  if (rc) return rc;
+  return a;
+}
+
+// The segments' partials -> per-row statistics -> trees.
+int launch_merge_and_tree(const CandArgs& a, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(a.cap) * (sizeof(double) + 2 * sizeof(int) + 2 * sizeof(float) + sizeof(int)) +
                       static_cast<size_t>(a.levels) * (static_cast<size_t>(a.top_k) * 12 + 4);
-  rc = a.kmax == 4 ? launch_merge_k<4>(a, st)
-                    : a.kmax == 8 ? launch_merge_k<8>(a, st)
-                                  : a.kmax == 16 ? launch_merge_k<16>(a, st) : launch_merge_k<32>(a, st);
+  int rc = a.kmax == 4 ? launch_merge_k<4>(a, st)
+                        : a.kmax == 8 ? launch_merge_k<8>(a, st)
+                                      : a.kmax == 16 ? launch_merge_k<16>(a, st) : launch_merge_k<32>(a, st);
   if (rc) return rc;
   if (smem > 48 * 1024) {
     rc = check_cuda(cudaFuncSetAttribute(cand_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -800,6 +1060,117 @@ extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void
                     "candidate-tree smem attribute");
     if (rc) return rc;
   }
-  cand_tree_kernel<<<static_cast<unsigned>(p->batch), 32, smem, st>>>(a);
+  cand_tree_kernel<<<static_cast<unsigned>(a.batch), 32, smem, st>>>(a);
   return check_cuda(cudaGetLastError(), "candidate-tree launch");
+}
+
+template <typename T, int NB, int K>
+int launch_head_k(const CandArgs& a, const HeadArgs& h, cudaStream_t st) {
+  auto kern = head_segment_kernel<T, NB, K>;
+  const size_t smem = static_cast<size_t>(NB) * h.hidden * sizeof(T);
+  if (smem > 48 * 1024) {
+    const int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(smem)),
+                              "fused head smem attribute");
+    if (rc) return rc;
+  }
+  kern<<<dim3(static_cast<unsigned>(a.segs), static_cast<unsigned>(a.levels)), kHeadThreads, smem, st>>>(a, h);
+  return check_cuda(cudaGetLastError(), "fused head segment launch");
+}
+
+template <typename T, int NB>
+int launch_head_nb(const CandArgs& a, const HeadArgs& h, cudaStream_t st) {
+  if (a.kmax == 4) return launch_head_k<T, NB, 4>(a, h, st);
+  if (a.kmax == 8) return launch_head_k<T, NB, 8>(a, h, st);
+  if (a.kmax == 16) return launch_head_k<T, NB, 16>(a, h, st);
+  return launch_head_k<T, NB, 32>(a, h, st);
+}
+
+template <typename T>
+int launch_head_t(const CandArgs& a, const HeadArgs& h, cudaStream_t st) {
+  if (a.batch == 1) return launch_head_nb<T, 1>(a, h, st);
+  if (a.batch == 2) return launch_head_nb<T, 2>(a, h, st);
+  return launch_head_nb<T, 4>(a, h, st);
+}
+
+}  // namespace
+}  // namespace gorgon
+
+extern "C" size_t gorgon_candidate_tree_workspace_size(const gorgon_candidate_tree_params* p) {
+  using namespace gorgon;
+  if (!p || p->batch <= 0 || p->levels <= 0 || p->top_k <= 0 || p->vocab <= 0 || !dtype_ok(p->dtype)) return 0;
+  return workspace_bytes(p, segments(p->dtype, p->vocab));
+}
+
+extern "C" int gorgon_candidate_tree(const gorgon_candidate_tree_params* p, void* workspace, size_t workspace_bytes_,
+                                     void* stream) {
+  using namespace gorgon;
+  if (!p) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: params is null");
+  const int64_t segs = p->vocab > 0 && dtype_ok(p->dtype) ? segments(p->dtype, p->vocab) : 0;
+  int rc = check_tree(p, segs, "gorgon_candidate_tree");
+  if (rc) return rc == 1 ? GORGON_OK : rc;
+  if (!p->logits) return set_error(GORGON_ERR_INVALID, "gorgon_candidate_tree: null pointer");
+  if (!workspace || workspace_bytes_ < workspace_bytes(p, segs))
+    return set_error(GORGON_ERR_WORKSPACE, "gorgon_candidate_tree: workspace too small");
+  const CandArgs a = make_args(p, segs, static_cast<char*>(workspace));
+  const int rows = a.batch * a.levels;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->dtype == GORGON_F32) rc = launch_stats_t<float>(a, rows, st);
+  else if (p->dtype == GORGON_BF16) rc = launch_stats_t<__nv_bfloat16>(a, rows, st);
+  else rc = launch_stats_t<__half>(a, rows, st);
+  if (rc) return rc;
+  return launch_merge_and_tree(a, st);
+}
+
+extern "C" size_t gorgon_head_candidate_tree_workspace_size(const gorgon_head_candidate_params* p) {
+  using namespace gorgon;
+  if (!p) return 0;
+  const gorgon_candidate_tree_params* t = &p->tree;
+  if (t->batch <= 0 || t->levels <= 0 || t->top_k <= 0 || t->vocab <= 0 || !dtype_ok(t->dtype)) return 0;
+  return workspace_bytes(t, head_segments(t->vocab, t->levels));
+}
+
+extern "C" int gorgon_head_candidate_tree(const gorgon_head_candidate_params* p, void* workspace,
+                                          size_t workspace_bytes_, void* stream) {
+  using namespace gorgon;
+  constexpr const char* kWho = "gorgon_head_candidate_tree";
+  if (!p) return set_error(GORGON_ERR_INVALID, "gorgon_head_candidate_tree: params is null");
+  const gorgon_candidate_tree_params* t = &p->tree;
+  const int64_t segs = t->vocab > 0 && t->levels > 0 ? head_segments(t->vocab, t->levels) : 0;
+  int rc = check_tree(t, segs, kWho);
+  if (rc) return rc == 1 ? GORGON_OK : rc;
+  if (p->x_dtype != GORGON_BF16 && p->x_dtype != GORGON_F16)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_head_candidate_tree: hidden and lm_head must be bf16 or f16");
+  if (t->batch > kHeadMaxBatch)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_head_candidate_tree: batch must be <= 4");
+  if (p->hidden_size < 8 || p->hidden_size > kHeadMaxHidden || p->hidden_size % 8)
+    return set_error(GORGON_ERR_UNSUPPORTED,
+                     "gorgon_head_candidate_tree: hidden_size must be a multiple of 8 in [8, 8192]");
+  if (!p->hidden || !p->lm_head) return set_error(GORGON_ERR_INVALID, "gorgon_head_candidate_tree: null pointer");
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!al16(p->hidden) || p->hidden_stride_b % 8 || p->hidden_stride_l % 8 || p->lm_head_stride_v % 8 ||
+      p->lm_head_stride_v < p->hidden_size)
+    return set_error(GORGON_ERR_INVALID,
+                     "gorgon_head_candidate_tree: hidden and lm_head rows must be 16-byte aligned, strides "
+                     "multiples of 8 elements, lm_head rows at least hidden_size apart");
+  HeadArgs h{};
+  for (int64_t l = 0; l < t->levels; ++l) {
+    if (!p->lm_head[l] || !al16(p->lm_head[l]))
+      return set_error(GORGON_ERR_INVALID, "gorgon_head_candidate_tree: an lm_head pointer is null or unaligned");
+    h.w[l] = p->lm_head[l];
+  }
+  if (!workspace || workspace_bytes_ < workspace_bytes(t, segs))
+    return set_error(GORGON_ERR_WORKSPACE, "gorgon_head_candidate_tree: workspace too small");
+  h.x = p->hidden;
+  h.xsb = p->hidden_stride_b;
+  h.xsl = p->hidden_stride_l;
+  h.wsv = p->lm_head_stride_v;
+  h.hidden = static_cast<int>(p->hidden_size);
+  h.seg_rows = static_cast<int>(head_seg_rows(t->vocab, t->levels));
+  h.logit_dtype = t->dtype;
+  const CandArgs a = make_args(t, segs, static_cast<char*>(workspace));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = p->x_dtype == GORGON_BF16 ? launch_head_t<__nv_bfloat16>(a, h, st) : launch_head_t<__half>(a, h, st);
+  if (rc) return rc;
+  return launch_merge_and_tree(a, st);
 }

@@ -151,3 +151,16 @@ def test_golden_candidate_cases_cover_every_rule():
     for n in ("k3_threshold", "k5_threshold_entropy", "k4_threshold_path", "k4_all_rules"):
         full = sum(int(CAND[f"{n}_params"][0]) ** (l + 1) for l in range(int(CAND[f"{n}_depth"])))
         assert 0 < sizes[n] < full, n
+
+
+def test_head_logits_rounding_matches_torch():
+    """The oracle's bf16 / f16 rounding of a head's logits is torch's."""
+    import torch
+    rng = np.random.default_rng(4)
+    h = rng.standard_normal((2, 64)).astype(np.float32)
+    ws = [rng.standard_normal((300, 64)).astype(np.float32) for _ in range(2)]
+    exact = O.head_logits(h, ws)
+    ref = np.stack([w.astype(np.float64) @ h[l].astype(np.float64) for l, w in enumerate(ws)]).astype(np.float32)
+    assert np.array_equal(exact, ref)
+    assert np.array_equal(O.head_logits(h, ws, "bf16"), torch.from_numpy(ref).bfloat16().float().numpy())
+    assert np.array_equal(O.head_logits(h, ws, "f16"), torch.from_numpy(ref).half().float().numpy())
