@@ -55,6 +55,10 @@ NCU_TRAFFIC_BYTES = {
     ("candidates-b32-h4-v128256", "cand_segment_kernel"): 32893440,
     # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 2181.164 MB read + 7.039 MB written
     ("wide-b8-p32k-n256", "tcgen05"): 2188202976,
+    # profiles/head_segment_kernel_medusa-heads-b1-h4-d4096-v128256.md: the one-head capture
+    # (1050.718 MB read + 3.665 MB written) and, scaled by the head count, the four-head workload
+    ("medusa-heads-b1-h1-d4096-v128256", "head_segment_kernel"): 1054383104,
+    ("medusa-heads-b1-h4-d4096-v128256", "head_segment_kernel"): 4217532416,
 }
 
 WORKLOADS = {
@@ -85,6 +89,14 @@ WORKLOADS = {
     # per-head top-4, softmax and entropy, then a 64-node budgeted tree
     "candidates-b32-h4-v128256": dict(kind="cand", B=32, heads=4, V=128256, top_k=4, max_candidates=64,
                                       dtype="bf16"),
+    # the same trees straight from 4 Medusa heads' last Linear (Llama-3-8B
+    # width: 4096 x 128256 bf16 per head, 4.2 GB of weights), one sequence
+    "medusa-heads-b1-h4-d4096-v128256": dict(kind="heads", B=1, heads=4, H=4096, V=128256, top_k=4,
+                                             max_candidates=64, dtype="bf16"),
+    # one such head (1.05 GB of weights): small enough for a multi-pass
+    # profiler capture; its traffic scales with the head count
+    "medusa-heads-b1-h1-d4096-v128256": dict(kind="heads", B=1, heads=1, H=4096, V=128256, top_k=4,
+                                             max_candidates=64, dtype="bf16"),
 }
 DEFAULT_WORKLOAD = "verify-b16-p8192-n64"
 TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
@@ -595,10 +607,128 @@ class CandidateWorkload:
                            f"top-k, softmax, entropy) and build_candidate_tree, extrapolated to the batch")}
 
 
+class HeadsWorkload:
+    """Candidate trees from the Medusa heads' last Linear with the logits
+    never stored (gorgon_head_candidate_tree): every head's lm_head weight
+    [V, H] bf16 streams from HBM once per step, the logits of the batch's
+    head inputs are computed and reduced to top-k, softmax and entropy in the
+    same kernel, then the trees are assembled.  The weights (4.2 GB) are far
+    larger than L2, so no flush is needed between steps."""
+
+    metric = "fused Medusa heads HBM GB/s (lm_head weight bytes / step time)"
+    data = "synthetic (seeded N(0, 0.02) bf16 lm_head weights, N(0, 1) bf16 head inputs)"
+    bound = "hbm"
+    flush_l2 = False
+
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
+        cfg = WORKLOADS[name]
+        self.name, self.cfg, self.dev = name, cfg, dev
+        B, L, H, V = cfg["B"], cfg["heads"], cfg["H"], cfg["V"]
+        self.w = []
+        for l in range(L):
+            w = torch.empty(V, H, device=dev, dtype=torch.bfloat16)
+            _fill_normal(w, torch.Generator(device=dev).manual_seed(5_000_011 + l), 0.02)
+            self.w.append(w)
+        self.x = torch.empty(B, L, H, device=dev, dtype=torch.bfloat16)
+        for j in range(B):
+            _fill_normal(self.x[j], torch.Generator(device=dev).manual_seed(6_000_007 + first_seq + j), 1.0)
+        self.cap = G.inference.max_tree_nodes(cfg["top_k"], L, V, cfg["max_candidates"])
+        self.bytes = L * V * H * 2 + B * L * H * 2 + B * (self.cap * (8 + 4 + 4) + 4)
+        self.flops = 2 * B * L * V * H
+        self.tokens = B * self.cap
+
+    def step(self):
+        c = self.cfg
+        return G.inference.head_candidate_trees(self.x, self.w, top_k=c["top_k"], max_candidates=c["max_candidates"])
+
+    def plan(self):
+        return {"backend": "head_segment_kernel", "splits": None, "launches": 3}
+
+    def config(self, world: int, plan: dict) -> dict:
+        c = self.cfg
+        return {"workload": self.name, "batch_per_gpu": c["B"], "heads": c["heads"], "hidden": c["H"],
+                "vocab": c["V"], "top_k": c["top_k"], "max_candidates": c["max_candidates"],
+                "weights_dtype": "bf16", "logits_dtype": "bf16 (rounded in the kernel, never stored)",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "inputs larger than L2 (4.2 GB of weights per step)", "backend": plan["backend"]}
+
+    def extra(self, world: int, ms_step: float) -> dict:
+        c = self.cfg
+        out = {"us_per_step": round(ms_step * 1e3, 2),
+               "trees_built_per_s": round(world * c["B"] / (ms_step * 1e-3), 1)}
+        # the same step unfused: cuBLAS GEMMs write the logits, the candidate kernels read them
+        L = c["heads"]
+
+        def unfused():
+            lg = torch.stack([self.x[:, l] @ self.w[l].T for l in range(L)], dim=1)
+            return G.build_candidate_trees(lg, top_k=c["top_k"], max_candidates=c["max_candidates"])
+        ms_u = _time_loop(unfused, self.dev, 10, 3, 1) / 10
+        out["unfused_us_per_step"] = round(ms_u * 1e3, 2)
+        return out
+
+    def e2e(self, steps: int, warmup: int, world: int):
+        """Each step: the head inputs copied in from pinned host memory, the
+        trees built, their tokens, parents and node counts copied out (the
+        weights stay resident, as a model's do)."""
+        B, L, H = self.cfg["B"], self.cfg["heads"], self.cfg["H"]
+        x_h = self.x.cpu().pin_memory()
+        tok_h = torch.empty(B, self.cap, dtype=torch.int64).pin_memory()
+        par_h = torch.empty(B, self.cap, dtype=torch.int32).pin_memory()
+        n_h = torch.empty(B, dtype=torch.int32).pin_memory()
+        d2h = tok_h.numel() * 8 + par_h.numel() * 4 + n_h.numel() * 4
+
+        def one():
+            self.x.copy_(x_h, non_blocking=True)
+            t = self.step()
+            tok_h.copy_(t.tokens, non_blocking=True)
+            par_h.copy_(t.parents, non_blocking=True)
+            n_h.copy_(t.n_nodes, non_blocking=True)
+
+        ms = _time_loop(one, self.dev, steps, warmup, world)
+        return ms, B * L * H * 2, d2h, "lm_head weights resident in HBM; head inputs in, trees out through pinned host memory"
+
+    def cpu_baseline(self, budget_s: float):
+        return heads_cpu_sample(self.cfg, budget_s)
+
+
+def heads_cpu_sample(cfg: dict, budget_s: float) -> dict:
+    """The oracle on the host: head_logits (float64 matrix-vector products
+    through numpy's BLAS) over a 16384-row slice of one head's weights,
+    extrapolated to every row of every head and sequence, plus one
+    sequence's head_topk and build_candidate_tree on full-width logits."""
+    from oracle import gorgon_oracle as O
+    B, L, H, V, k, mc = cfg["B"], cfg["heads"], cfg["H"], cfg["V"], cfg["top_k"], cfg["max_candidates"]
+    rng = np.random.default_rng(0)
+    rows = 16384
+    w = rng.standard_normal((rows, H)) * 0.02
+    x = rng.standard_normal((1, H))
+    lg_full = rng.standard_normal((L, V), dtype=np.float32) * 2.0
+    t_g, t_c, n = [], [], 0
+    t_start = time.perf_counter()
+    while n < 3 or time.perf_counter() - t_start < min(budget_s, 5.0):
+        t0 = time.perf_counter()
+        O.head_logits(x, [w], "bf16")
+        t_g.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        levels = [O.head_topk(lg_full[h], k) for h in range(L)]
+        O.build_candidate_tree(levels, k, max_candidates=mc)
+        t_c.append(time.perf_counter() - t0)
+        n += 1
+        if time.perf_counter() - t_start > budget_s:
+            break
+    step_s = (float(np.mean(t_g)) * (V / rows) * L + float(np.mean(t_c))) * B
+    wl_bytes = L * V * H * 2 + B * L * H * 2 + B * (min(sum(k ** (i + 1) for i in range(L)), mc) * 16 + 4)
+    return {"value": round(wl_bytes / step_s / 1e9, 4), "unit": "GB/s", "cores": blas_threads(), "kind": "port",
+            "us_per_step": round(step_s * 1e6, 1),
+            "sample": (f"{n} runs of the oracle's head_logits over a {rows}-row slice of one head (float64 "
+                       f"BLAS), extrapolated to {L} heads x {V} rows x {B} sequence(s), plus head_topk and "
+                       f"build_candidate_tree of one sequence")}
+
+
 def make_workload(name: str, dev: torch.device, first_seq: int = 0):
     kind = WORKLOADS[name].get("kind", "attn")
     return {"attn": Workload, "verify": VerifyWorkload, "trim": TrimWorkload,
-            "cand": CandidateWorkload}[kind](name, dev, first_seq)
+            "cand": CandidateWorkload, "heads": HeadsWorkload}[kind](name, dev, first_seq)
 
 
 # --------------------------------------------------------------------------
@@ -1054,6 +1184,24 @@ def run_reference_other(args, cfg: dict, world: int):
     rng = np.random.default_rng(0)
     prng = random.Random(0)
     B, N = cfg["B"], cfg.get("N", 0)
+    if cfg["kind"] == "heads":
+        for _ in range(max(args.warmup, 1)):
+            heads_cpu_sample(cfg, 1.0)
+        runs = [heads_cpu_sample(cfg, 5.0) for _ in range(args.steps)]
+        step_us = float(np.mean([r["us_per_step"] for r in runs]))
+        value = float(np.mean([r["value"] for r in runs]))
+        cb = dict(runs[-1], value=round(value, 4))
+        cb.pop("us_per_step", None)
+        out = {
+            "impl": "reference", "metric": HeadsWorkload.metric, "value": round(value, 4), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_us / 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic", "config": {"workload": args.workload, "batch_per_gpu": B},
+            "cpu_baseline": cb,
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(out), flush=True)
+        return
     if cfg["kind"] == "cand":
         L, V, k, mc = cfg["heads"], cfg["V"], cfg["top_k"], cfg["max_candidates"]
         cap = min(sum(k ** (i + 1) for i in range(L)), mc)
