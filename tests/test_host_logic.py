@@ -56,6 +56,16 @@ def test_fused_and_verify_reject_host_tensors():
         G.accept_draft_tokens([1, 2], torch.randn(2, 5))
 
 
+def test_candidate_builders_reject_host_tensors():
+    from projectgorgon_b200.inference import build_candidate_trees, head_candidate_trees
+    with pytest.raises(ValueError):
+        build_candidate_trees(torch.randn(1, 2, 100))
+    x = torch.zeros(1, 2, 64, dtype=torch.bfloat16)
+    w = [torch.zeros(100, 64, dtype=torch.bfloat16)] * 2
+    with pytest.raises(ValueError):
+        head_candidate_trees(x, w)
+
+
 def test_verify_oracle_preorder_rule_on_random_trees():
     """The kernel's selection rule (deepest accepted node, first in preorder)
     equals the reference's path loop, checked on the oracle."""
