@@ -463,13 +463,28 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
   drain_wait(&bars->drain[1], 0);
 }
 
+// Visibility of 64 consecutive key columns for one row: bit j is set when
+// column (tree index o + j) is visible -- a prefix column (tree index < 0) or
+// an ancestor of the row's node (bit set in anc).  Built once per masked
+// tile with a funnel shift of the ancestor words, so that masking a column
+// costs a constant-bit test instead of a run-time compare-and-select chain
+// per column (the per-column form made the masked tile the slowest tile of
+// a unit by several microseconds).
 template <int ANCW>
-__device__ __forceinline__ bool anc_bit(const uint32_t (&anc)[ANCW], int t) {
-  uint32_t w = 0;
+__device__ __forceinline__ uint64_t vis_window(const uint32_t (&anc)[ANCW], int o) {
+  if (o <= -64) return ~0ull;
+  // word w of the extended bit array: all ones before the tree, 0 after the last word
+  auto word = [&](int w) -> uint32_t {
+    uint32_t r = w < 0 ? 0xffffffffu : 0u;
 #pragma unroll
-  for (int k = 0; k < ANCW; ++k)
-    if ((t >> 5) == k) w = anc[k];
-  return (w >> (t & 31)) & 1u;
+    for (int k = 0; k < ANCW; ++k) r = (w == k) ? anc[k] : r;
+    return r;
+  };
+  const int w0 = o >> 5;  // floor(o / 32), also for negative o
+  const int sh = o & 31;
+  const uint64_t lo = static_cast<uint64_t>(word(w0)) | (static_cast<uint64_t>(word(w0 + 1)) << 32);
+  const uint64_t hi = word(w0 + 2);
+  return sh == 0 ? lo : (lo >> sh) | (hi << (64 - sh));
 }
 
 // All 32 lanes wait; the result is the same on every lane.
@@ -606,6 +621,18 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
       constexpr bool kMask = decltype(mask_tag)::value;
       const uint32_t buf = static_cast<uint32_t>(i & 1);
       const uint32_t bi = buf * MT + wg;
+      // masked tiles: the row's visibility words, before S fills the registers
+      // (columns past the sequence are tree indices >= n, whose ancestor bits are 0)
+      uint32_t vw[kBN / 32];
+      if (kMask) {
+        const int o = static_cast<int>(g - pi.start) * kBN - P;
+#pragma unroll
+        for (int hh = 0; hh < kBN / 64; ++hh) {
+          const uint64_t w = len_ok ? vis_window<ANCW>(anc, o + 64 * hh) : 0ull;
+          vw[2 * hh] = static_cast<uint32_t>(w);
+          vw[2 * hh + 1] = static_cast<uint32_t>(w >> 32);
+        }
+      }
       if (!warp_wait(&bars->s_full[bi], static_cast<uint32_t>(i >> 1) & 1u, abort)) return false;
       tc_fence_after();
       const uint32_t s_addr = lane_base + kColS + bi * kBN;
@@ -621,14 +648,8 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
           for (int c = 0; c < 32; ++c) x[32 * q + c] = __uint_as_float(rr[q][c]);
       }
       if (kMask) {
-        const int c0 = static_cast<int>(g - pi.start) * kBN;
 #pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const int col = c0 + c;
-          const int tt = col - P;
-          const bool vis = len_ok && col < pi.L && (tt < 0 || anc_bit<ANCW>(anc, tt));
-          x[c] = vis ? x[c] : -INFINITY;
-        }
+        for (int c = 0; c < kBN; ++c) x[c] = ((vw[c >> 5] >> (c & 31)) & 1u) ? x[c] : -INFINITY;
       }
       // row max of the raw scores (scale > 0, so it commutes with max)
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
