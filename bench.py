@@ -44,8 +44,10 @@ from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tre
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
 NCU_TRAFFIC_BYTES = {
-    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.588 MB read + 5.126 MB written
-    ("verify-b16-p8192-n64", "tcgen05"): 554714112,
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.552 MB read + 3.763 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 553314560,
+    # profiles/attn_tc_kernel_verify-b1-p2048-n64.md: 9.273 MB read, 0 written
+    ("verify-b1-p2048-n64", "tcgen05"): 9273088,
     # profiles/verify_kernel_verifier-b32-n64-v128256.md: 572.339 MB read + 3.123 MB written
     ("verifier-b32-n64-v128256", "verify_kernel"): 575461632,
     # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
@@ -99,6 +101,7 @@ WORKLOADS = {
                                              max_candidates=64, dtype="bf16"),
 }
 DEFAULT_WORKLOAD = "verify-b16-p8192-n64"
+L2_FLUSH_BELOW = 256e6  # bytes per step under which a workload flushes L2 between steps
 TORCH_DT = {"bf16": torch.bfloat16, "fp32": torch.float32}
 
 
@@ -170,6 +173,8 @@ class Workload:
                       + ((B + 1) * 4 if self.ragged else 0))
         self.flops = 4 * Hq * N * D * kv_rows
         self.tokens = B * N
+        # a layer that fits in L2 (126 MB) twice over is timed from a flushed L2
+        self.flush_l2 = self.bytes < L2_FLUSH_BELOW
 
     def kwargs(self):
         kw = dict(parents=self.par_t, max_depth=self.max_depth)
@@ -198,7 +203,8 @@ class Workload:
             "tree_nodes": cfg["N"], "tree": cfg["tree"], "max_depth": self.max_depth,
             "mask": "parents (mask-free)",
             "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-            "l2": f"inputs larger than L2 ({self.bytes / 1e6:.0f} MB per step per GPU)",
+            "l2": ("L2 flushed before every step (a 256 MB write outside the step's events)" if self.flush_l2
+                   else f"inputs larger than L2 ({self.bytes / 1e6:.0f} MB per step per GPU)"),
             "backend": plan["backend"], "splits": plan["splits"],
         }
 
