@@ -55,8 +55,8 @@ NCU_TRAFFIC_BYTES = {
     ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11108352,
     # profiles/cand_segment_kernel_candidates-b32-h4-v128256.md: 32.893 MB read, 0 written
     ("candidates-b32-h4-v128256", "cand_segment_kernel"): 32893440,
-    # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 2181.164 MB read + 7.039 MB written
-    ("wide-b8-p32k-n256", "tcgen05"): 2188202976,
+    # profiles/attn_tc_kernel_wide-b8-p32k-n256.md: 1100.020 MB read + 16.812 MB written
+    ("wide-b8-p32k-n256", "tcgen05"): 1116831744,
     # profiles/head_segment_kernel_medusa-heads-b1-h4-d4096-v128256.md: the one-head capture
     # (1050.718 MB read + 3.665 MB written) and, scaled by the head count, the four-head workload
     ("medusa-heads-b1-h1-d4096-v128256", "head_segment_kernel"): 1054383104,
