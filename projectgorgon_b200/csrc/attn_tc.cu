@@ -1122,17 +1122,6 @@ struct Plan {
   bool varlen, pair_align;
 };
 
-// Two M-tiles per CTA unless the 256-row units would leave most SMs idle.
-// Measured on B200 (bf16, 32 q / 8 kv heads, 64-node trees): with whole units
-// filling the GPU, MT = 2 is the faster shape (16 x 8192 prefix: 158 us
-// against 184 for MT = 1; 256-node trees over 32k: 1142 against 1351 us;
-// ragged 16 x 1k-8k: 172 against 209 us); on a single sequence (8 units of
-// 256 rows, 2048 prefix) MT = 1 wins, 43 against 47 us.
-int choose_mt(const AttnArgs& a) {
-  const int units2 = a.batch * a.hkv * ((a.group * a.n + 2 * kBM - 1) / (2 * kBM));
-  return units2 * 4 <= sm_count() ? 1 : 2;
-}
-
 template <int MT>
 Plan make_plan_mt(const AttnArgs& a) {
   using C = Cfg<MT>;
@@ -1181,7 +1170,26 @@ Plan make_plan_mt(const AttnArgs& a) {
   return pl;
 }
 
-Plan make_plan(const AttnArgs& a) { return choose_mt(a) == 1 ? make_plan_mt<1>(a) : make_plan_mt<2>(a); }
+// The CTA shape: two M-tiles (K/V staged once for 256 rows) or one (128-key
+// tiles, twice the units).  Whole units filling the GPU beat any split, so a
+// shape whose plan is whole units wins, MT = 2 first; between two split
+// plans, MT = 2 once the work per SM is large (its K/V staging pays), MT = 1
+// below (less fixed work per piece): the MT = 2 tile count per SM crosses
+// over between 14 and 28.  Measured on B200 (bf16, 32 q / 8 kv heads,
+// 64-node trees, CUDA graphs, us, MT = 1 against MT = 2): 8 x 2048 28.5 /
+// 38.6 and 8 x 4096 46.7 / 54.7 (MT = 1 whole units); 2 x 8192 34.3 / 37.2
+// and 1 x 2048 19.3 / 22.3 (split, few tiles); 4 x 8192 53.4 / 50.7 and
+// 2 x 16384 53.0 / 51.1 (split, many tiles); 16 x 8192 159.4 / 148.4 and
+// 256-node trees over 8 x 32k 1351 / 1142 (MT = 2 whole units).
+Plan make_plan(const AttnArgs& a) {
+  const Plan p2 = make_plan_mt<2>(a);
+  if (p2.pair_align) return p2;
+  const Plan p1 = make_plan_mt<1>(a);
+  if (p1.pair_align) return p1;
+  const int64_t units2 = static_cast<int64_t>(a.batch) * a.hkv * ((a.group * a.n + 2 * kBM - 1) / (2 * kBM));
+  const int64_t tiles2 = units2 * ((static_cast<int64_t>(a.kv_len) + Cfg<2>::kBN - 1) / Cfg<2>::kBN);
+  return tiles2 <= 20LL * sm_count() ? p1 : p2;
+}
 
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
