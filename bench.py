@@ -48,8 +48,8 @@ NCU_TRAFFIC_BYTES = {
     ("verify-b16-p8192-n64", "tcgen05"): 553314560,
     # profiles/attn_tc_kernel_verify-b1-p2048-n64.md: 9.273 MB read, 0 written
     ("verify-b1-p2048-n64", "tcgen05"): 9273088,
-    # profiles/verify_kernel_verifier-b32-n64-v128256.md: 572.339 MB read + 3.123 MB written
-    ("verifier-b32-n64-v128256", "verify_kernel"): 575461632,
+    # profiles/verify_kernel_verifier-b32-n64-v128256.md: 570.646 MB read + 4.049 MB written
+    ("verifier-b32-n64-v128256", "verify_kernel"): 574694912,
     # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
     # 0 written) scaled by 8 to 32 layers
     ("kvtrim-b32-l32-p4096", "kv_trim_kernel"): 11108352,

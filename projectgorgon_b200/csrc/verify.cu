@@ -87,7 +87,7 @@ __device__ __forceinline__ void scan_chunks16(const uint4* __restrict__ rv, int6
   using P = typename PT::P;
   float rm = -INFINITY;
   int64_t rc = -1;
-  constexpr int U = 4;
+  constexpr int U = 8;
   int64_t v = threadIdx.x;
   auto fold = [&](const uint4& raw, int64_t idx) {
     const P* p = reinterpret_cast<const P*>(&raw);
@@ -147,7 +147,7 @@ __device__ __forceinline__ void scan_row(const T* __restrict__ row, int64_t voca
   if (vec_ok) {
     const int64_t nvec = vocab / EV;
     const uint4* rv = reinterpret_cast<const uint4*>(row);
-    constexpr int U = 4;
+    constexpr int U = 8;
     int64_t v = threadIdx.x;
     for (; v + (U - 1) * kThreads < nvec; v += U * kThreads) {
       uint4 raw[U];
