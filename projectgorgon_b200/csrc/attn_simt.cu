@@ -57,21 +57,34 @@ __device__ __forceinline__ void load_rows(float* dst, int dst_stride, const T* _
   constexpr int EV = 16 / sizeof(T);
   if (vec_ok) {
     constexpr int VPR = DMAX / EV;  // vectors per row
-    for (int idx = threadIdx.x; idx < rows * VPR; idx += kThreads) {
-      const int r = idx / VPR;
-      const int c0 = (idx % VPR) * EV;
-      float vals[EV];
-      if (r < rows_valid && c0 < d) {
-        const uint4 raw = *reinterpret_cast<const uint4*>(src + row0_off + r * row_stride + c0);
-        const T* e = reinterpret_cast<const T*>(&raw);
+    // Up to 8 vectors per thread are requested before any is converted and
+    // stored, so a tile costs one or two memory round trips instead of one
+    // per vector (31-node bf16 trees over 16 x 8192: 4611 -> 3265 us).  The
+    // 256-wide variant keeps one at a time: its accumulators leave no
+    // registers for more without losing a resident CTA (68 -> 81 us with 8).
+    constexpr int kBatch = DMAX > 128 ? 1 : 8;
+    const int total = rows * VPR;
+    for (int base = 0; base < total; base += kBatch * kThreads) {
+      uint4 raw[kBatch];
 #pragma unroll
-        for (int u = 0; u < EV; ++u) vals[u] = Cvt<T>::to_f(e[u]) * mul;
-      } else {
-#pragma unroll
-        for (int u = 0; u < EV; ++u) vals[u] = 0.f;
+      for (int i = 0; i < kBatch; ++i) {
+        const int idx = base + i * kThreads + threadIdx.x;
+        const int r = idx / VPR;
+        const int c0 = (idx % VPR) * EV;
+        raw[i] = (idx < total && r < rows_valid && c0 < d)
+                     ? *reinterpret_cast<const uint4*>(src + row0_off + r * row_stride + c0)
+                     : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
-      for (int u = 0; u < EV; ++u) dst[r * dst_stride + c0 + u] = vals[u];
+      for (int i = 0; i < kBatch; ++i) {
+        const int idx = base + i * kThreads + threadIdx.x;
+        if (idx >= total) continue;
+        const int r = idx / VPR;
+        const int c0 = (idx % VPR) * EV;
+        const T* e = reinterpret_cast<const T*>(&raw[i]);
+#pragma unroll
+        for (int u = 0; u < EV; ++u) dst[r * dst_stride + c0 + u] = Cvt<T>::to_f(e[u]) * mul;
+      }
     }
   } else {
     for (int idx = threadIdx.x; idx < rows * DMAX; idx += kThreads) {
