@@ -304,9 +304,15 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnArgs a) {
   const float inv = 1.f / wsum;
   for (int col = lane; col < a.d; col += 32) {
     float o = 0.f;
+    // Every split's row is loaded (the workspace holds them all) and a zero
+    // weight selects it away, rather than branching around the load, so the
+    // unrolled splits' loads are in flight together; an empty split's row
+    // never reaches the sum.
+#pragma unroll 4
     for (int s = 0; s < a.splits; ++s) {
       const float w = exp2f(a.part_lse[s * total + row] - M);
-      if (w > 0.f) o = fmaf(w, a.part_o[(s * total + row) * a.d + col], o);
+      const float v = a.part_o[(s * total + row) * a.d + col];
+      o = w > 0.f ? fmaf(w, v, o) : o;
     }
     store_as(a.out, a.out_dtype, ob + col, o * inv);
   }
