@@ -6,17 +6,21 @@ The default workload is the Llama-3-8B layer shape: batch 16, 32 query / 8
 key-value heads, head_dim 128, prefix 8192, a 64-node random tree per
 sequence (depth <= 5), bf16.
 
-Prints one JSON line (rank 0).  ``value`` is algorithmic HBM GB/s summed over
-all GPUs (K and V of every sequence read once, Q read once, output written
+Prints one JSON line (rank 0).  ``value`` is algorithmic HBM GB/s of the
+whole job (K and V of every sequence read once, Q read once, output written
 once, parents read once) with inputs resident in HBM; ``e2e`` is the same
 metric with each step's new inputs (Q, the tree's K/V rows, parents) copied
-from pinned host memory and the output copied back inside the timed region.
+from pinned host memory and the output copied back inside the timed region,
+with the time each stage takes on its own stream.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-    python bench.py --impl reference ...   # the CPU oracle port on host cores
+    python bench.py --impl reference ...   # the reference's attention on the host cores
 
-Multi-GPU (torchrun, one rank per GPU): each rank verifies its own batch of
-sequences (weak scaling by sequence); the timing is the max over ranks.
+Multi-GPU (torchrun, one rank per GPU): by default the workload's batch is
+split by sequence over the ranks (strong scaling: the same layer on more
+GPUs, no collective on the data path); ``--shard weak`` gives every rank a
+batch of its own, ``--shard heads`` splits one layer by kv head with an NCCL
+all-gather of the output.  The timing is the max over ranks.
 """
 from __future__ import annotations
 
@@ -72,6 +76,9 @@ WORKLOADS = {
                                  tree="cartesian", max_depth=31),
     "ragged-b16-p1k-8k-n64": dict(B=16, Hq=32, Hkv=8, D=128, P=(1024, 8192), N=64, dtype="bf16",
                                   tree="random", max_depth=5),
+    # one layer of the 32-layer verify tail: 32 sequences over a 4096-token prefix
+    "verify-b32-p4096-n64": dict(B=32, Hq=32, Hkv=8, D=128, P=4096, N=64, dtype="bf16",
+                                 tree="random", max_depth=5),
     # 256-node best-first trees (top-4 over 4 levels) over a 32k prefix: the
     # tensor-bound shape (arithmetic intensity ~1000 flop/byte)
     "wide-b8-p32k-n256": dict(B=8, Hq=32, Hkv=8, D=128, P=32768, N=256, dtype="bf16",
@@ -118,6 +125,89 @@ def make_tree(cfg: dict, rng: random.Random):
     return cartesian_tree(4, 2, True)
 
 
+def attn_sequences(cfg: dict, first_seq: int, count: int):
+    """(prefix lengths, parents) of global sequences first_seq .. first_seq +
+    count - 1.  Sequence j's prefix and tree come from a generator seeded by
+    j alone, so any split of the batch over ranks (or the host-side
+    reference) sees the same job."""
+    prefixes, parents = [], []
+    for j in range(first_seq, first_seq + count):
+        r = random.Random(1_000_003 + j)
+        prefixes.append(r.randint(*cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"])
+        parents.append(make_tree(cfg, r))
+    return prefixes, parents
+
+
+def attn_bytes(cfg: dict, prefixes) -> int:
+    """Algorithmic HBM bytes of the attention over these sequences: K and V of
+    every kv head read once over P + N rows, Q read once, the output written
+    once, parents (and cu_seqlens for a ragged batch) read once."""
+    B, Hq, Hkv, D, N = len(prefixes), cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"]
+    esz = 2 if cfg["dtype"] == "bf16" else 4
+    kv_rows = sum(p + N for p in prefixes)
+    return (2 * kv_rows * Hkv * D * esz + 2 * B * Hq * N * D * esz + B * N * 4
+            + ((B + 1) * 4 if isinstance(cfg["P"], tuple) else 0))
+
+
+def attn_flops(cfg: dict, prefixes) -> int:
+    """Dense-equivalent FLOPs: 4 * Hq * N * D per key/value row (Q.K^T and P.V)."""
+    return 4 * cfg["Hq"] * cfg["N"] * cfg["D"] * sum(p + cfg["N"] for p in prefixes)
+
+
+def seq_shard(name: str, world: int, rank: int, mode: str):
+    """(first sequence, sequence count) of `rank`.  ``strong``: the workload's
+    fixed batch split over the ranks (contiguous runs; a ragged batch is cut
+    by key/value rows so every rank streams about the same bytes); ``weak``:
+    every rank takes a whole batch of its own."""
+    cfg = WORKLOADS[name]
+    B = cfg["B"]
+    if mode == "weak" or world == 1:
+        return rank * B if mode == "weak" else 0, B
+    if B < world:
+        raise SystemExit(f"{name}: {B} sequences cannot be split over {world} ranks (use --shard weak)")
+    if cfg.get("kind", "attn") == "attn" and isinstance(cfg["P"], tuple):
+        prefixes, _ = attn_sequences(cfg, 0, B)
+        s, e = sharding.shard_by_weight([p + cfg["N"] for p in prefixes], world, rank)
+    else:
+        s, e = sharding.shard_range(B, world, rank)
+    return s, e - s
+
+
+def attn_config(name: str, world: int, mode: str) -> dict:
+    """The `config` of an attention workload's JSON line: the same dict for
+    this build's arm and the reference arm (it needs no GPU)."""
+    cfg = WORKLOADS[name]
+    ragged = isinstance(cfg["P"], tuple)
+    B = cfg["B"]
+    if mode in ("weak", "heads") or world == 1:
+        per_gpu = [B] * world
+        local_bytes = attn_bytes(cfg, attn_sequences(cfg, 0, B)[0]) // (world if mode == "heads" else 1)
+    else:
+        per_gpu = [seq_shard(name, world, r, mode)[1] for r in range(world)]
+        s0, n0 = seq_shard(name, world, 0, mode)
+        local_bytes = attn_bytes(cfg, attn_sequences(cfg, s0, n0)[0])
+    if world == 1:
+        par = "single GPU"
+    elif mode == "weak":
+        par = f"sequence-sharded x{world}, weak scaling: {B} sequences per GPU, {B * world} in all"
+    elif mode == "heads":
+        par = (f"kv-head-sharded x{world}, strong scaling: {cfg['Hkv'] // world} of {cfg['Hkv']} kv heads per GPU, "
+               f"one NCCL all-gather of the output")
+    else:
+        par = (f"sequence-sharded x{world}, strong scaling: the batch of {B} sequences split "
+               f"{'/'.join(str(n) for n in per_gpu)} over the GPUs, no collective on the data path")
+    return {
+        "workload": name, "batch": B * world if mode == "weak" else B,
+        "batch_per_gpu": per_gpu[0] if len(set(per_gpu)) == 1 else per_gpu,
+        "heads_q": cfg["Hq"], "heads_kv": cfg["Hkv"], "head_dim": cfg["D"],
+        "prefix": list(cfg["P"]) if ragged else cfg["P"], "tree_nodes": cfg["N"], "tree": cfg["tree"],
+        "max_depth": cfg["max_depth"], "mask": "parents (mask-free)", "parallelism": par,
+        "l2": ("L2 flushed before every step (a 256 MB write outside the step's events)"
+               if local_bytes < L2_FLUSH_BELOW else
+               f"inputs larger than L2 ({local_bytes / 1e6:.0f} MB per step per GPU)"),
+    }
+
+
 # --------------------------------------------------------------------------
 # workload construction
 # --------------------------------------------------------------------------
@@ -129,14 +219,14 @@ class Workload:
     global index, so the union of all ranks' shards is one well-defined job
     whatever the number of ranks."""
 
-    def __init__(self, name: str, dev: torch.device, first_seq: int = 0):
+    def __init__(self, name: str, dev: torch.device, first_seq: int = 0, batch: int = None):
         cfg = WORKLOADS[name]
         self.name, self.cfg, self.dev = name, cfg, dev
-        B, Hq, Hkv, D, N = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"]
+        B = cfg["B"] if batch is None else batch
+        Hq, Hkv, D, N = cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"]
+        self.B, self.first_seq = B, first_seq
         self.ragged = isinstance(cfg["P"], tuple)
-        rngs = [random.Random(1_000_003 + first_seq + j) for j in range(B)]
-        self.prefixes = [r.randint(*cfg["P"]) if self.ragged else cfg["P"] for r in rngs]
-        self.parents = [make_tree(cfg, r) for r in rngs]
+        self.prefixes, self.parents = attn_sequences(cfg, first_seq, B)
         self.max_depth = cfg["max_depth"]
         dt = TORCH_DT[cfg["dtype"]]
         self.dtype = dt
@@ -167,11 +257,8 @@ class Workload:
                 self.v[j] = (torch.randn(Hkv, L, D, device=dev, generator=gens[j]) * s).to(dt)
             self.max_seqlen = L
         self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
-        esz = torch.tensor([], dtype=dt).element_size()
-        kv_rows = sum(p + N for p in self.prefixes)
-        self.bytes = (2 * kv_rows * Hkv * D * esz + 2 * B * Hq * N * D * esz + B * N * 4
-                      + ((B + 1) * 4 if self.ragged else 0))
-        self.flops = 4 * Hq * N * D * kv_rows
+        self.bytes = attn_bytes(cfg, self.prefixes)
+        self.flops = attn_flops(cfg, self.prefixes)
         self.tokens = B * N
         # a layer that fits in L2 (126 MB) twice over is timed from a flushed L2
         self.flush_l2 = self.bytes < L2_FLUSH_BELOW
@@ -195,28 +282,25 @@ class Workload:
     def bound(self):
         return self.cfg.get("bound", "hbm")
 
+    mode = "strong"
+
     def config(self, world: int, plan: dict) -> dict:
-        cfg = self.cfg
-        return {
-            "workload": self.name, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"], "heads_kv": cfg["Hkv"],
-            "head_dim": cfg["D"], "prefix": cfg["P"] if not self.ragged else list(cfg["P"]),
-            "tree_nodes": cfg["N"], "tree": cfg["tree"], "max_depth": self.max_depth,
-            "mask": "parents (mask-free)",
-            "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-            "l2": ("L2 flushed before every step (a 256 MB write outside the step's events)" if self.flush_l2
-                   else f"inputs larger than L2 ({self.bytes / 1e6:.0f} MB per step per GPU)"),
-            "backend": plan["backend"], "splits": plan["splits"],
-        }
+        return attn_config(self.name, world, self.mode)
 
     def extra(self, world: int, ms_step: float) -> dict:
         return {"us_per_layer": round(ms_step * 1e3, 2),
-                "tokens_verified_per_s": round(world * self.tokens / (ms_step * 1e-3), 1)}
+                "tokens_verified_per_s": round(self.job_tokens(world) / (ms_step * 1e-3), 1)}
+
+    def job_tokens(self, world: int) -> int:
+        """Tree tokens verified per step by all ranks together."""
+        return self.cfg["B"] * self.cfg["N"] * (world if self.mode == "weak" else 1)
 
     def e2e(self, steps: int, warmup: int, world: int):
-        ms, h2d, d2h = time_e2e(self, steps, warmup, world)
+        ms, h2d, d2h, parts = time_e2e(self, steps, warmup, world)
         return ms, h2d, d2h, ("prefix K/V cache resident in HBM; per step the tree's Q, K/V rows and "
                               "parents are copied in and the output copied out, pipelined: step i + 1's "
-                              "copy-in and step i - 1's copy-out overlap step i's compute")
+                              "copy-in and step i - 1's copy-out overlap step i's compute; the *_ms parts "
+                              "are each stage's mean duration on its own stream"), parts
 
     def cpu_baseline(self, budget_s: float):
         return cpu_baseline(self, budget_s=budget_s)
@@ -263,7 +347,10 @@ class HeadShardWorkload(Workload):
                 self.k[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
                 self.v[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
         self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
-        self.out = torch.empty(B, Hq, N, D, device=dev, dtype=dt)
+        # the layer output, head-major: this rank's heads are one contiguous
+        # chunk that the attention writes and the in-place all-gather sends
+        self.full, self.local = sharding.head_sharded_output(B, Hq, N, D, dt, dev, world, rank)
+        self.out = self.full.permute(1, 0, 2, 3)
         esz = torch.tensor([], dtype=dt).element_size()
         # this rank's share: its K/V, Q and output slice, and the parents
         self.bytes = 2 * B * (h1 - h0) * L * D * esz + 2 * B * (q1 - q0) * N * D * esz + B * N * 4
@@ -275,21 +362,16 @@ class HeadShardWorkload(Workload):
         st = torch.cuda.current_stream(self.dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        o = G.fused_tree_verify(self.q, self.k, self.v, **self.kwargs())
+        G.fused_tree_verify(self.q, self.k, self.v, out=self.local, **self.kwargs())
         e1.record(st)
         self.kernel_events.append((e0, e1))
-        return sharding.gather_heads(o, self.out)
+        return sharding.gather_heads_inplace(self.full)
 
     def post(self, o):
         """The output gather of one e2e step (a fresh buffer per step)."""
         return sharding.gather_heads(o)
 
-    def config(self, world: int, plan: dict) -> dict:
-        c = super().config(world, plan)
-        c["parallelism"] = f"kv-head-sharded x{world}, NCCL all-gather of the output" if world > 1 else "single GPU"
-        c["batch"] = c.pop("batch_per_gpu")
-        c["shard"] = "heads"
-        return c
+    mode = "heads"
 
     def extra(self, world: int, ms_step: float) -> dict:
         ev = self.kernel_events[-min(len(self.kernel_events), 50):]
@@ -741,19 +823,22 @@ def make_workload(name: str, dev: torch.device, first_seq: int = 0):
 # clocks during the timed region
 # --------------------------------------------------------------------------
 class ClockSampler:
-    """Samples SM clock and clock-event reasons of one GPU every few ms while
-    the timed region runs (NVML; falls back to nvidia-smi when absent)."""
+    """Samples SM clock and clock-event reasons of one GPU every 0.5 ms while
+    the timed region runs (NVML), so that even a timed region of a few
+    milliseconds carries several samples."""
 
     REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
                0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, dev: torch.device, period_s: float = 0.005):
+    def __init__(self, dev: torch.device, period_s: float = 0.0005):
         self.dev, self.period = dev, period_s
         self.samples = []
         self.max_mhz = None
         self._stop = threading.Event()
         self._thread = None
         self._nvml = None
+        self._sample = None
+        self._last_poll = 0.0
 
     def _handle(self):
         import pynvml
@@ -774,21 +859,34 @@ class ClockSampler:
             get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
                                   getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
 
+            def sample():
+                try:
+                    mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                    rs = int(get_reasons(h)) if get_reasons else 0
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+
             def run():
                 while not self._stop.is_set():
-                    try:
-                        mhz = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                        rs = int(get_reasons(h)) if get_reasons else 0
-                        self.samples.append((mhz, rs))
-                    except Exception:
-                        pass
+                    sample()
                     self._stop.wait(self.period)
 
+            self._sample = sample
             self._thread = threading.Thread(target=run, daemon=True)
             self._thread.start()
         except Exception as exc:  # pragma: no cover - NVML missing
             log(f"clock sampling unavailable: {exc}")
         return self
+
+    def poll(self):
+        """One sample from the calling thread (the timing loop calls it right
+        after launching a step, while the GPU still has queued work), at most
+        one per sampling period so the launches stay ahead of the GPU."""
+        now = time.perf_counter()
+        if self._sample is not None and now - self._last_poll >= self.period:
+            self._last_poll = now
+            self._sample()
 
     def __exit__(self, *exc):
         self._stop.set()
@@ -809,26 +907,8 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------
-# CPU baseline: the oracle port (numpy / BLAS) on a bounded sample
+# CPU baseline: the reference's attention on whole sequences, host cores
 # --------------------------------------------------------------------------
-def cpu_slices(cfg: dict, count: int, seed: int = 0):
-    """`count` random (batch, q-head) slices of a workload, generated on the
-    host with the workload's shapes and distributions: (q [N, D], k, v
-    [P_b + N, D], mask [N, P_b + N], kv rows) in float32."""
-    from oracle import gorgon_oracle as O
-    rng = np.random.default_rng(seed)
-    prng = random.Random(seed)
-    N, D = cfg["N"], cfg["D"]
-    s = 1.0 / math.sqrt(D)
-    for _ in range(count):
-        P = prng.randint(*cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"]
-        par = make_tree(cfg, prng)
-        q = (rng.standard_normal((N, D), dtype=np.float32) * s)
-        k = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
-        v = (rng.standard_normal((P + N, D), dtype=np.float32) * s)
-        yield q, k, v, O.prefix_tree_mask(par, P, cfg["max_depth"]), P + N
-
-
 def use_all_host_threads() -> None:
     """Lets numpy's BLAS use every host thread (torchrun sets OMP_NUM_THREADS=1
     for each rank; the reference arm runs on rank 0 alone)."""
@@ -847,39 +927,29 @@ def blas_threads() -> int:
         return os.cpu_count() or 1
 
 
-def mean_kv_rows(cfg: dict) -> float:
-    if isinstance(cfg["P"], tuple):
-        return (cfg["P"][0] + cfg["P"][1]) / 2 + cfg["N"]
-    return cfg["P"] + cfg["N"]
-
-
-def cpu_baseline(wl: "Workload", budget_s: float = 12.0, max_slices: int = 64):
-    """Times the oracle's tree_attention on (batch, query-head) slices of the
-    workload for about `budget_s` seconds and extrapolates to the full layer
-    by key/value rows."""
-    from oracle import gorgon_oracle as O
-    cfg = wl.cfg
-    cores = blas_threads()
-    total_slices = cfg["B"] * cfg["Hq"]
-    times, rows = [], 0
-    t_start = time.perf_counter()
-    for q, k, v, m, L in cpu_slices(cfg, max_slices, seed=1):
+def cpu_baseline(wl: "Workload", budget_s: float = 12.0):
+    """The reference's mask + attention (``HostAttention``) on whole sequences
+    of the workload, run one after another on the host cores until about
+    `budget_s` seconds have passed (at least one sequence); the rate is the
+    bytes of the sequences run over the time they took."""
+    ha = HostAttention(wl.name)
+    ha.run_seq(0)  # warm-up
+    done, secs, nbytes = 0, 0.0, 0
+    while done < wl.cfg["B"] and (done == 0 or secs < budget_s):
         t0 = time.perf_counter()
-        O.tree_attention(q, k, v, m)
-        times.append(time.perf_counter() - t0)
-        rows += L
-        if time.perf_counter() - t_start > budget_s:
-            break
-    layer_s = sum(times) / rows * (sum(p + cfg["N"] for p in wl.prefixes) / cfg["B"]) * total_slices
+        ha.run_seq(done)
+        secs += time.perf_counter() - t0
+        nbytes += ha.seq_bytes(done)
+        done += 1
     return {
-        "value": round(wl.bytes / layer_s / 1e9, 4),
+        "value": round(nbytes / secs / 1e9, 4),
         "unit": "GB/s",
-        "cores": cores,
-        "kind": "port",
-        "us_per_layer": round(layer_s * 1e6, 1),
-        "sample": (f"{len(times)} of {total_slices} (batch, q-head) slices of this workload, "
-                   f"oracle tree_attention in fp32 numpy/BLAS on {cores} threads, "
-                   f"extrapolated by kv rows to the full layer"),
+        "cores": ha.cores,
+        "kind": ha.kind,
+        "us_per_layer": round(secs / done * wl.cfg["B"] * 1e6, 1),
+        "sample": (f"{done} of the {wl.cfg['B']} sequences of this workload (all {wl.cfg['Hq']} query heads), "
+                   f"{ha.origin} with its build_tree_mask on {ha.cores} host threads; us_per_layer scales "
+                   f"the measured time to the whole batch"),
     }
 
 
@@ -914,6 +984,7 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
             starts[i].record(st)
             wl.step()
             ends[i].record(st)
+            clk.poll()
         torch.cuda.synchronize(dev)
     total_ms = starts[0].elapsed_time(ends[-1])
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
@@ -966,24 +1037,42 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     in_free = [torch.cuda.Event() for _ in range(nbuf)]
     done = [torch.cuda.Event() for _ in range(nbuf)]
     kw = wl.kwargs()
+    # per-step stamps of each stage, on the stream that runs it: copy-in (both
+    # copy streams), compute (the tree rows' cache write and the attention),
+    # copy-out; read after the loop, so they cost no synchronisation
+    stamps = []
 
-    def one(i):
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def one(i, rec):
         k = i % nbuf
         q_d, kt_d, vt_d, par_d = bufs[k]
+        st = [ev() for _ in range(8)] if rec else None
         with torch.cuda.stream(s_in):
             if i >= nbuf:
                 s_in.wait_event(in_free[k])  # step i - 2 has read this buffer set
+            if rec:
+                st[0].record(s_in)
             q_d.copy_(q_h, non_blocking=True)
+            if rec:
+                st[1].record(s_in)
             in_ready[k].record(s_in)
         with torch.cuda.stream(s_in2):
             if i >= nbuf:
                 s_in2.wait_event(in_free[k])
+            if rec:
+                st[2].record(s_in2)
             kt_d.copy_(kt_h, non_blocking=True)
             vt_d.copy_(vt_h, non_blocking=True)
             par_d.copy_(par_h, non_blocking=True)
+            if rec:
+                st[3].record(s_in2)
             in_ready2[k].record(s_in2)
         s_c.wait_event(in_ready[k])
         s_c.wait_event(in_ready2[k])
+        if rec:
+            st[4].record(s_c)
         if wl.ragged:
             wl.k[rows] = kt_d
             wl.v[rows] = vt_d
@@ -993,33 +1082,55 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
         o = G.fused_tree_verify(q_d, wl.k, wl.v, **dict(kw, parents=par_d))
         if post is not None:
             o = post(o)
+        if rec:
+            st[5].record(s_c)
         in_free[k].record(s_c)
         done[k].record(s_c)
         with torch.cuda.stream(s_out):
             s_out.wait_event(done[k])
+            if rec:
+                st[6].record(s_out)
             outs_h[k].copy_(o, non_blocking=True)
+            if rec:
+                st[7].record(s_out)
             o.record_stream(s_out)
+        if rec:
+            stamps.append(st)
 
-    def run(n):
+    def run(n, rec):
         for i in range(n):
-            one(i)
+            one(i, rec)
         s_c.wait_stream(s_in)
         s_c.wait_stream(s_in2)
         s_c.wait_stream(s_out)
 
-    run(warmup)
+    run(warmup, False)
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = ev(), ev()
     e0.record(s_c)
     s_in.wait_event(e0)
     s_in2.wait_event(e0)
     s_out.wait_event(e0)
-    run(steps)
+    t_host = time.perf_counter()
+    run(steps, False)
+    t_host = time.perf_counter() - t_host
     e1.record(s_c)
     torch.cuda.synchronize(dev)
-    return e0.elapsed_time(e1), h2d, d2h
+    total = e0.elapsed_time(e1)
+    # a second, instrumented pass gives each stage's own duration
+    run(min(steps, 50), True)
+    torch.cuda.synchronize(dev)
+    cin = float(np.mean([max(a[0].elapsed_time(a[1]), a[2].elapsed_time(a[3])) for a in stamps]))
+    comp = float(np.mean([a[4].elapsed_time(a[5]) for a in stamps]))
+    cout = float(np.mean([a[6].elapsed_time(a[7]) for a in stamps]))
+    parts = {"copy_in_ms": round(cin, 5), "compute_ms": round(comp, 5), "copy_out_ms": round(cout, 5),
+             "host_issue_ms": round(t_host * 1e3 / steps, 5),
+             "h2d_gbs": round(h2d / (cin * 1e-3) / 1e9, 2), "d2h_gbs": round(d2h / (cout * 1e-3) / 1e9, 2),
+             "bound": max((("copy-in", cin), ("compute", comp), ("copy-out", cout),
+                           ("host issue", t_host * 1e3 / steps)), key=lambda x: x[1])[0]}
+    return total, h2d, d2h, parts
 
 
 def _time_loop(one, dev, steps: int, warmup: int, world: int) -> float:
@@ -1059,32 +1170,43 @@ def run_ours(args):
         raise SystemExit("bench.py needs a CUDA device")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    # NCCL's version banner goes to stdout, where rank 0's JSON line must be alone
-    os.environ["NCCL_DEBUG"] = "WARN"
     sharding.init(sharding.dist_env(), "nccl", dev, timeout_s=120)
     G.load_library()
-    # weak scaling by sequence: rank r verifies global sequences [r*B, (r+1)*B)
+    kind = WORKLOADS[args.workload].get("kind", "attn")
     if args.shard == "heads":
-        if WORKLOADS[args.workload].get("kind", "attn") != "attn":
+        if kind != "attn":
             raise SystemExit("--shard heads applies to the attention workloads")
         wl = HeadShardWorkload(args.workload, dev, rank, world)
+    elif kind == "attn":
+        # strong (default): the fixed batch split over the ranks; weak: a batch per rank
+        mode = "weak" if args.shard == "weak" else "strong"
+        first, count = seq_shard(args.workload, world, rank, mode)
+        wl = Workload(args.workload, dev, first_seq=first, batch=count)
+        wl.mode = mode
     else:
+        # the other workloads run a whole batch per rank
         wl = make_workload(args.workload, dev, first_seq=rank * WORKLOADS[args.workload]["B"])
+        wl.mode = "weak"
     plan = wl.plan()
+    # bytes of the whole job: every rank's share (weak: every rank's batch)
+    job_bytes = int(sharding.sum_over_ranks(wl.bytes, dev)) if world > 1 else wl.bytes
     total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
     total_ms = max_over_ranks(total_ms, world, dev)
     launch_ms = max_over_ranks(launch_ms, world, dev)
-    e2e_steps = args.e2e_steps or args.steps
-    e2e_ms, h2d, d2h, e2e_note = wl.e2e(e2e_steps, args.warmup, world)
+    e2e_steps = args.e2e_steps or max(100, args.steps)
+    e2e = wl.e2e(e2e_steps, args.warmup, world)
+    e2e_ms, h2d, d2h, e2e_note = e2e[:4]
+    e2e_parts = e2e[4] if len(e2e) > 4 else None
     e2e_ms = max_over_ranks(e2e_ms, world, dev)
+    extra = wl.extra(world, total_ms / args.steps)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
     ms_step = total_ms / args.steps
-    value = world * wl.bytes * args.steps / (total_ms * 1e-3) / 1e9
-    e2e_val = world * wl.bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    value = job_bytes * args.steps / (total_ms * 1e-3) / 1e9
+    e2e_val = job_bytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
     hbm_peak, tc_peak, peak_kind = peaks()
     if wl.bound == "tensor":
         achieved = wl.flops / (launch_ms * 1e-3) / 1e12
@@ -1101,8 +1223,14 @@ def run_ours(args):
                 else "fallback 6650 GB/s"}
         if wl.flops:
             roof["tflops"] = round(wl.flops / (launch_ms * 1e-3) / 1e12, 2)
-    roof.update({"traffic": NCU_TRAFFIC_BYTES.get((wl.name, plan["backend"])),
-                 "launch_us": round(launch_ms * 1e3, 3), "algorithmic_bytes": wl.bytes})
+    roof.update({"traffic": NCU_TRAFFIC_BYTES.get((wl.name, plan["backend"])) if world == 1 else None,
+                 "launch_us": round(launch_ms * 1e3, 3), "algorithmic_bytes": wl.bytes,
+                 "per": "one GPU's launch (the slowest rank's mean)" if world > 1 else "the launch"})
+    e2e_out = {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 5), "steps": e2e_steps,
+               "note": e2e_note}
+    if e2e_parts:
+        e2e_out.update(e2e_parts)
     out = {
         "metric": wl.metric,
         "value": round(value, 2),
@@ -1112,69 +1240,157 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 5),
         "higher_is_better": True,
-        "scaling": getattr(wl, "scaling", "weak"),
+        "scaling": "weak" if wl.mode == "weak" else "strong",
         "vs_baseline": None,
         "dtype": wl.cfg["dtype"],
         "data": wl.data,
         "config": wl.config(world, plan),
+        "plan": {"backend": plan["backend"], "splits": plan.get("splits"), "launches_per_step": plan["launches"]},
         "pct_of_8tbs": round(100.0 * value / world / 8000.0, 2),
         "roofline": roof,
-        "e2e": {
-            "value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / e2e_steps, 5), "note": e2e_note,
-        },
+        "e2e": e2e_out,
         "gpu_launches": plan["launches"] * args.steps,
         "clocks": clocks,
     }
-    out.update(wl.extra(world, ms_step))
+    out.update(extra)
     if world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = wl.cpu_baseline(args.cpu_budget)
     print(json.dumps(out), flush=True)
 
 
+def reference_attention():
+    """(attention(q, k, v, mask), mask(parents, depth), kind, origin): the
+    reference's own ``tree_attention_ref`` (torch on the host cores,
+    ``src/gorgon/kernels/tree_attention_ref.py:8-18``) and ``build_tree_mask``
+    (``src/gorgon/kernels/tree_mask.py:16-44``) from its unmodified install
+    under ``baseline/_ref``; without that install, the oracle's numpy
+    restatement of the same two functions."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "gorgon" / "kernels" / "tree_attention_ref.py").exists():
+        if str(ref_dir) not in sys.path:
+            sys.path.insert(0, str(ref_dir))
+        from gorgon.kernels.tree_attention_ref import tree_attention_ref
+        from gorgon.kernels.tree_mask import build_tree_mask
+
+        def mask(parents, depth):
+            return build_tree_mask(list(parents), depth=depth)
+        return tree_attention_ref, mask, "reference", "the reference's tree_attention_ref (torch, fp32)"
+    from oracle import gorgon_oracle as O
+
+    def attn_np(q, k, v, m):
+        return O.tree_attention(q.numpy(), k.numpy(), v.numpy(), m.numpy())
+
+    def mask_np(parents, depth):
+        return torch.from_numpy(O.build_tree_mask(parents, depth))
+    return attn_np, mask_np, "port", "the oracle's tree_attention (numpy, fp32; reference install absent)"
+
+
+def host_threads() -> int:
+    """Every host thread for torch and BLAS (torchrun sets OMP_NUM_THREADS=1
+    per rank; the reference arm runs on rank 0 alone)."""
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    use_all_host_threads()
+    return n
+
+
+class HostAttention:
+    """The reference's verify attention on the host over whole sequences of
+    an attention workload: per sequence its tree mask (``build_tree_mask``
+    of the parents, ``max_depth`` hops, after a fully visible prefix), then
+    ``tree_attention_ref`` for each query head over its kv head's P + N rows,
+    in fp32 on the same seeded sequences the GPU arm runs (inputs drawn
+    N(0, 1)/sqrt(d) and rounded to bf16 first for bf16 workloads)."""
+
+    def __init__(self, name: str):
+        self.name, self.cfg = name, WORKLOADS[name]
+        self.attn, self.mask, self.kind, self.origin = reference_attention()
+        self.cores = host_threads()
+        self._cache = {}
+
+    def seq_inputs(self, j: int):
+        if j not in self._cache:
+            cfg = self.cfg
+            (P,), (par,) = attn_sequences(cfg, j, 1)
+            N, D, Hq, Hkv = cfg["N"], cfg["D"], cfg["Hq"], cfg["Hkv"]
+            g = torch.Generator().manual_seed(7_000_003 + j)
+            s = 1.0 / math.sqrt(D)
+
+            def draw(*shape):
+                x = torch.randn(*shape, generator=g) * s
+                return x.bfloat16().float() if cfg["dtype"] == "bf16" else x
+            self._cache[j] = (draw(Hq, N, D), draw(Hkv, P + N, D), draw(Hkv, P + N, D), par, P)
+        return self._cache[j]
+
+    def run_seq(self, j: int) -> None:
+        cfg = self.cfg
+        q, k, v, par, P = self.seq_inputs(j)
+        N, G_ = cfg["N"], cfg["Hq"] // cfg["Hkv"]
+        tm = torch.as_tensor(self.mask(par, cfg["max_depth"]), dtype=torch.bool)
+        m = torch.cat([torch.ones(N, P, dtype=torch.bool), tm], dim=1)
+        for h in range(cfg["Hq"]):
+            self.attn(q[h], k[h // G_], v[h // G_], m)
+
+    def seq_bytes(self, j: int) -> int:
+        return attn_bytes(self.cfg, [self.seq_inputs(j)[4]])
+
+    def plan_step(self, target_s: float) -> int:
+        """Sequences per step: as many whole sequences as fit in about
+        `target_s` seconds (at least one, at most the batch)."""
+        self.run_seq(0)
+        t0 = time.perf_counter()
+        self.run_seq(0)
+        t_seq = time.perf_counter() - t0
+        return int(max(1, min(self.cfg["B"], target_s // max(t_seq, 1e-6))))
+
+
 def run_reference(args):
-    """CPU oracle port on the host cores, same metric and workload.  Each step
-    is one (batch, q-head) slice; the layer time is extrapolated by kv rows."""
+    """The reference arm on the host cores, same metric, workload and config
+    as this build's arm.  Each step runs whole sequences of the workload --
+    the full batch when it fits in about two seconds, else the first few --
+    through the reference's own mask and attention functions, and is timed
+    as it runs: nothing is extrapolated."""
     world, rank, _ = dist_setup()
     if rank != 0:
         return
-    use_all_host_threads()
-    from oracle import gorgon_oracle as O
     cfg = WORKLOADS[args.workload]
     if cfg.get("kind", "attn") != "attn":
+        use_all_host_threads()
         run_reference_other(args, cfg, world)
         return
-    cores = blas_threads()
-    inputs = list(cpu_slices(cfg, 8, seed=0))
-    total_slices = cfg["B"] * cfg["Hq"]
-    esz = 2 if cfg["dtype"] == "bf16" else 4
-    rows = mean_kv_rows(cfg)
-    layer_bytes = (2 * rows * cfg["B"] * cfg["Hkv"] * cfg["D"] * esz
-                   + 2 * cfg["B"] * cfg["Hq"] * cfg["N"] * cfg["D"] * esz + cfg["B"] * cfg["N"] * 4)
-    for i in range(args.warmup):
-        O.tree_attention(*inputs[i % len(inputs)][:4])
-    t_layer = []
-    for i in range(args.steps):
-        q, k, v, m, L = inputs[i % len(inputs)]
+    ha = HostAttention(args.workload)
+    per_step = ha.plan_step(2.0)
+    seqs = list(range(per_step))
+    for j in seqs:
+        ha.seq_inputs(j)
+    step_bytes = sum(ha.seq_bytes(j) for j in seqs)
+    for _ in range(args.warmup):
+        for j in seqs:
+            ha.run_seq(j)
+    times = []
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.tree_attention(q, k, v, m)
-        t_layer.append((time.perf_counter() - t0) / L * rows * total_slices)
-    layer_s = float(np.mean(t_layer))
-    value = layer_bytes / layer_s / 1e9
+        for j in seqs:
+            ha.run_seq(j)
+        times.append(time.perf_counter() - t0)
+    step_s = float(np.mean(times))
+    value = step_bytes / step_s / 1e9
+    mode = "weak" if args.shard == "weak" else ("heads" if args.shard == "heads" else "strong")
+    what = (f"each step {per_step} of the {cfg['B']} sequences of the workload (all {cfg['Hq']} query heads "
+            f"over each one's full prefix + tree): {ha.origin} with its build_tree_mask, on "
+            f"{ha.cores} host threads, timed per step")
     out = {
         "impl": "reference",
-        "metric": "tree-verify HBM GB/s (algorithmic bytes / step time)",
+        "metric": Workload.metric,
         "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(layer_s * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic",
-        "config": {"workload": args.workload, "batch_per_gpu": cfg["B"], "heads_q": cfg["Hq"],
-                   "heads_kv": cfg["Hkv"], "head_dim": cfg["D"],
-                   "prefix": list(cfg["P"]) if isinstance(cfg["P"], tuple) else cfg["P"],
-                   "tree_nodes": cfg["N"]},
-        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": "each step one (batch, q-head) slice of the workload through the "
-                                   "oracle's tree_attention (fp32 numpy/BLAS), extrapolated by kv "
-                                   "rows to the full layer"},
+        "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak" if mode == "weak" else "strong", "vs_baseline": None, "dtype": cfg["dtype"],
+        "data": Workload.data,
+        "config": attn_config(args.workload, world, mode),
+        "sequences_per_step": per_step,
+        "us_per_layer": round(step_s * 1e6 * cfg["B"] / per_step, 1),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": ha.cores, "kind": ha.kind,
+                         "sample": what},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
@@ -1278,12 +1494,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--e2e-steps", type=int, default=0, help="steps of the e2e loop (default: --steps)")
+    ap.add_argument("--e2e-steps", type=int, default=0,
+                    help="steps of the e2e loop (default: the larger of --steps and 100)")
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"],
-                    help="multi-GPU split: whole sequences per rank (weak scaling, default) or one layer's "
-                         "kv heads per rank with an NCCL all-gather of the output (strong scaling)")
+    ap.add_argument("--shard", default="sequences", choices=["sequences", "weak", "heads"],
+                    help="multi-GPU split: the workload's batch divided by sequence over the ranks (strong "
+                         "scaling, default), a whole batch per rank (weak scaling), or one layer's kv heads "
+                         "per rank with an NCCL all-gather of the output (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()

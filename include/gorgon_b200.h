@@ -200,6 +200,9 @@ GORGON_API int gorgon_verify(const gorgon_verify_params* p, void* workspace,
  * - Every call clears the counters it uses on `stream` first.  All calls
  *   share the one array, so calls that overlap on the GPU (on different
  *   streams at the same time) race; keep them ordered on one stream.
+ * - The looked-up address is kept for the life of the process: the library
+ *   must not outlive a reset of the device (cudaDeviceReset, or the primary
+ *   context torn down and created again); call nothing here after one.
  * - It allocates nothing: no cudaMalloc, cudaFree or allocating routine. */
 GORGON_API int gorgon_verify_noalloc(const gorgon_verify_params* p, void* stream);
 

@@ -387,7 +387,10 @@ int32_t* g_noalloc_counters[kNoAllocMaxDevices] = {};
 
 // Device address of the counter array on the current device.  Host code only
 // sees a stand-in for a __device__ symbol, so the address is looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process: a device reset (cudaDeviceReset, or a primary context destroyed
+// and created again) would leave the cached address stale, so the library
+// must not be used across one.
 int noalloc_counters(int32_t** out) {
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "gorgon_verify_noalloc: cudaGetDevice");

@@ -58,15 +58,19 @@ def tree_attention(
     return_lse: bool = False,
     backend: str = "auto",
     num_splits: int = 0,
+    out: Optional[torch.Tensor] = None,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Masked softmax attention of tree queries over prefix + tree keys.
 
     Exactly one of ``tree_mask`` and ``parents`` is given.  Returns ``out``
     shaped like ``q`` (dtype ``out_dtype`` or ``q.dtype``), and with
     ``return_lse`` also the natural-log sum-exp ``[B, Hq, N]`` (float32).
+    ``out``, when given, is written instead of a new tensor: 4-D ``q`` only,
+    shape ``[B, Hq, N, D]``, any strides with ``head_dim`` contiguous (e.g. a
+    head-major slice of a larger buffer).
     """
     prep = _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, scale,
-                    out_dtype, return_lse, backend, num_splits)
+                    out_dtype, return_lse, backend, num_splits, out)
     lib = _abi.lib()
     dev = prep.out.device
     with on_device(dev):
@@ -110,7 +114,7 @@ class _Prepared:
 
 
 def _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, scale, out_dtype,
-             return_lse, backend, num_splits) -> _Prepared:
+             return_lse, backend, num_splits, out=None) -> _Prepared:
     if (tree_mask is None) == (parents is None):
         raise RuntimeError("pass exactly one of tree_mask and parents")
     tensors = [q, k, v] + ([tree_mask] if tree_mask is not None else [])
@@ -124,7 +128,7 @@ def _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, sca
         common = torch.promote_types(torch.promote_types(q.dtype, k.dtype), v.dtype)
         q, k, v = q.to(common), k.to(common), v.to(common)
     dt = gorgon_dtype(q.dtype)
-    out_dt = out_dtype if out_dtype is not None else q.dtype
+    out_dt = out_dtype if out_dtype is not None else (out.dtype if out is not None else q.dtype)
     odt = gorgon_dtype(out_dt)
 
     q_shape = q.shape
@@ -156,7 +160,13 @@ def _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, sca
     if Hkv == 0 or Hq % Hkv != 0:
         raise RuntimeError(f"heads_q ({Hq}) must be a multiple of heads_kv ({Hkv})")
 
-    out = torch.empty((B, Hq, N, D), dtype=out_dt, device=dev)
+    if out is None:
+        out = torch.empty((B, Hq, N, D), dtype=out_dt, device=dev)
+    else:
+        if q.dim() != 4 or tuple(out.shape) != (B, Hq, N, D):
+            raise RuntimeError(f"out must be [B, Hq, N, D] = {(B, Hq, N, D)} for a 4-D q, got {tuple(out.shape)}")
+        if out.dtype != out_dt or out.device != dev or out.stride(-1) != 1:
+            raise RuntimeError("out must have the output dtype, q's device and a contiguous last dimension")
     lse = torch.empty((B, Hq, N), dtype=torch.float32, device=dev) if return_lse else None
     p = _abi.TreeAttnParams()
     p.dtype, p.out_dtype = dt, odt

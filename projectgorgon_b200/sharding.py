@@ -26,7 +26,7 @@ import torch
 import torch.distributed as dist
 
 __all__ = ["DistEnv", "dist_env", "init", "shard_range", "shard_by_weight", "shard_heads", "max_over_ranks",
-           "gather_batch", "gather_heads"]
+           "sum_over_ranks", "gather_batch", "gather_heads", "head_sharded_output", "gather_heads_inplace"]
 
 
 @dataclass(frozen=True)
@@ -116,6 +116,38 @@ def gather_heads(local: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
     return out
 
 
+def head_sharded_output(batch: int, heads_q: int, n: int, d: int, dtype: torch.dtype, device: torch.device,
+                        world: int, rank: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(full, local): the layer output held head-major -- a ``[Hq, B, N, D]``
+    buffer, so the query heads of rank r are one contiguous chunk -- and this
+    rank's ``[B, Hq / world, N, D]`` view of its own chunk, for the attention
+    to write straight into (``tree_attention(..., out=local)``).
+    :func:`gather_heads_inplace` then assembles the layer with one all-gather
+    and no re-layout copy."""
+    if world < 1 or not 0 <= rank < world or heads_q % world:
+        raise ValueError(f"{heads_q} query heads do not split evenly over {world} ranks")
+    per = heads_q // world
+    full = torch.empty((heads_q, batch, n, d), dtype=dtype, device=device)
+    return full, full[rank * per:(rank + 1) * per].permute(1, 0, 2, 3)
+
+
+def gather_heads_inplace(full: torch.Tensor) -> torch.Tensor:
+    """All-gathers a head-major output (:func:`head_sharded_output`) in place:
+    rank r's chunk is the send buffer and the whole buffer the receive buffer
+    (NCCL's in-place all-gather), so every rank ends with the layer's output.
+    Returns it as ``[B, Hq, N, D]`` (a view with head-major strides)."""
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        world, rank = dist.get_world_size(), dist.get_rank()
+        flat = full.view(-1)
+        chunk = flat.numel() // world
+        mine = flat[rank * chunk:(rank + 1) * chunk]
+        if dist.get_backend() == "nccl":
+            dist.all_gather_into_tensor(flat, mine)
+        else:
+            dist.all_gather(list(flat.view(world, chunk).unbind(0)), mine.clone())
+    return full.permute(1, 0, 2, 3)
+
+
 def max_over_ranks(value: float, device: torch.device = None) -> float:
     """The largest value any rank holds (the job's time is its slowest rank's)."""
     if not dist.is_initialized() or dist.get_world_size() == 1:
@@ -126,16 +158,48 @@ def max_over_ranks(value: float, device: torch.device = None) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(value: float, device: torch.device = None) -> float:
+    """The sum of every rank's value (e.g. the bytes of the whole job)."""
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return float(value)
+    t = torch.tensor([float(value)], dtype=torch.float64,
+                     device=device if device is not None else torch.device("cpu"))
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def gather_batch(local: torch.Tensor) -> torch.Tensor:
-    """Concatenates every rank's equally sized batch shard along dim 0."""
+    """Concatenates every rank's batch shard along dim 0, in rank order.
+
+    Shards may differ in length (``shard_range`` and ``shard_by_weight`` give
+    uneven runs when the batch does not divide): the ranks first exchange
+    their lengths, every shard is padded to the longest for one equal-sized
+    all-gather, and the padding is dropped.  The trailing dimensions must
+    agree on every rank."""
     if not dist.is_initialized() or dist.get_world_size() == 1:
         return local
     world = dist.get_world_size()
-    if dist.get_backend() == "nccl":
-        out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
-                          device=local.device)
-        dist.all_gather_into_tensor(out, local.contiguous())
-        return out
-    parts = [torch.empty_like(local) for _ in range(world)]
-    dist.all_gather(parts, local.contiguous())
-    return torch.cat(parts, 0)
+    nccl = dist.get_backend() == "nccl"
+    dev = local.device if nccl else torch.device("cpu")
+    lens = torch.zeros(world, dtype=torch.int64, device=dev)
+    mine = torch.tensor([local.shape[0]], dtype=torch.int64, device=dev)
+    if nccl:
+        dist.all_gather_into_tensor(lens, mine)
+    else:
+        dist.all_gather(list(lens.unbind(0)), mine[0].clone())
+    sizes = [int(x) for x in lens.cpu().tolist()]
+    most = max(sizes)
+    rest = tuple(local.shape[1:])
+    padded = local.contiguous()
+    if local.shape[0] < most:
+        padded = torch.cat([padded, padded.new_zeros((most - local.shape[0],) + rest)], 0)
+    if nccl:
+        allp = torch.empty((world * most,) + rest, dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(allp, padded)
+        parts = list(allp.split(most, 0))
+    else:
+        parts = [torch.empty_like(padded) for _ in range(world)]
+        dist.all_gather(parts, padded)
+    if all(n == most for n in sizes):
+        return torch.cat(parts, 0)
+    return torch.cat([p[:n] for p, n in zip(parts, sizes)], 0)

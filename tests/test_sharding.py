@@ -64,20 +64,28 @@ def _rank_main(rank, world, port, q):
     try:
         env = sharding.dist_env()
         sharding.init(env, "gloo", timeout_s=60)
-        # slowest rank's time is the job's time
+        # slowest rank's time is the job's time; the job's bytes are every rank's
         t = sharding.max_over_ranks(1.5 + rank)
-        # each rank holds its own sequences' outputs; the gather restores the batch order
-        B = 6
-        a, b = sharding.shard_range(B, world, rank)
-        full = torch.arange(B * 4, dtype=torch.float32).view(B, 4)
-        gathered = sharding.gather_batch(full[a:b].clone())
+        total = sharding.sum_over_ranks(10 + rank)
+        # each rank holds its own sequences' outputs; the gather restores the batch
+        # order, also when the shards differ in length (7 sequences: 3 and 4)
+        ok = total == 21.0
+        for B in (6, 7):
+            a, b = sharding.shard_range(B, world, rank)
+            full = torch.arange(B * 4, dtype=torch.float32).view(B, 4)
+            ok = ok and bool(torch.equal(sharding.gather_batch(full[a:b].clone()), full))
         # each rank holds the outputs of its query heads; the gather restores [B, Hq, N, D]
         o = torch.arange(3 * 8 * 5 * 2, dtype=torch.float32).view(3, 8, 5, 2)
         _, (q0, q1) = sharding.shard_heads(4, 8, world, rank)
-        heads = sharding.gather_heads(o[:, q0:q1].clone())
+        ok = ok and bool(torch.equal(sharding.gather_heads(o[:, q0:q1].clone()), o))
+        # head-major buffer: the rank writes its slice in place, the gather fills the rest
+        hm, local = sharding.head_sharded_output(3, 8, 5, 2, torch.float32, torch.device("cpu"), world, rank)
+        assert local.shape == (3, 4, 5, 2)
+        local.copy_(o[:, q0:q1])
+        ok = ok and bool(torch.equal(sharding.gather_heads_inplace(hm), o))
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-        q.put((rank, t, bool(torch.equal(gathered, full)) and bool(torch.equal(heads, o))))
+        q.put((rank, t, ok))
     except Exception as exc:  # pragma: no cover - reported to the parent
         q.put((rank, None, repr(exc)))
 
