@@ -55,7 +55,10 @@ typedef enum {
 typedef enum {
   GORGON_BACKEND_AUTO = 0,   /* tensor cores when the shape allows, else CUDA cores */
   GORGON_BACKEND_SIMT = 1,   /* CUDA-core split-K kernel (any head_dim <= 256, f32/bf16/f16) */
-  GORGON_BACKEND_TCGEN05 = 2 /* tcgen05 kernel (bf16/f16, head_dim 128) */
+  GORGON_BACKEND_TCGEN05 = 2, /* tcgen05 kernels (bf16/f16, head_dim 128); the planner picks the shape */
+  GORGON_BACKEND_TCGEN05_PAIR = 3, /* tcgen05 on CTA pairs (cta_group::2): whole 256-row units, uniform
+                                      kv length, 16-bit output rows of whole 16-byte chunks */
+  GORGON_BACKEND_TCGEN05_CTA = 4   /* tcgen05 on single CTAs (any tcgen05-capable shape) */
 } gorgon_backend;
 
 /* ABI version compiled into the library (GORGON_ABI_VERSION). */
@@ -67,9 +70,22 @@ GORGON_API const char* gorgon_last_error(void);
 /* Reads (synchronously) the device-side error word of the current device:
  * bit 0 = a parents[] entry outside [-1, n) was met, bit 1 = a KV-trim index
  * outside the cache, bit 2 = a verifier tree/draft entry out of range, bit 3 =
- * a candidate tree was cut at max_nodes.  The offending element is skipped,
- * never dereferenced.  clear != 0 resets it. */
+ * a sequence shorter than its tree, bit 4 = a bounded wait inside a
+ * tensor-core kernel ran out (the kernel stopped early and its outputs are
+ * incomplete), bit 5 = a candidate tree was cut at max_nodes.  The offending
+ * element is skipped, never dereferenced.  clear != 0 resets it. */
 GORGON_API int gorgon_device_error(uint32_t* out_flags, int clear);
+
+/* Sets the bound on every wait inside the tensor-core kernels (mbarrier
+ * waits on copies, MMAs and other warps), in nanoseconds of the GPU's global
+ * timer, for the whole process; ns <= 0 leaves it unchanged.  Returns the
+ * previous bound.  Default 2 s: far above any wait of a working kernel, so
+ * that only a stuck wait (a lost copy, a broken barrier) runs out; the CTA
+ * then stops, drains what it issued, frees its tensor memory and raises
+ * bit 4 of the device error word instead of hanging.  A very short bound
+ * makes ordinary waits run out too, which is how the test suite exercises
+ * that path.  No counterpart in the reference (its kernels have no waits). */
+GORGON_API int64_t gorgon_set_wait_limit_ns(int64_t ns);
 
 /* ------------------------------------------------------------------------
  * Tree mask.  Replaces build_tree_mask(parents, depth)

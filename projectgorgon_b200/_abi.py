@@ -22,12 +22,14 @@ GORGON_ERR_WORKSPACE = 4
 
 F32, BF16, F16 = 0, 1, 2
 MASK_PARENTS, MASK_DENSE, MASK_DENSE_TREE = 0, 1, 2
-BACKEND_AUTO, BACKEND_SIMT, BACKEND_TCGEN05 = 0, 1, 2
+BACKEND_AUTO, BACKEND_SIMT, BACKEND_TCGEN05, BACKEND_TCGEN05_PAIR, BACKEND_TCGEN05_CTA = 0, 1, 2, 3, 4
 
 ERR_BAD_PARENT = 1 << 0
 ERR_BAD_TRIM_INDEX = 1 << 1
 ERR_BAD_VERIFY_INPUT = 1 << 2
 ERR_BAD_SEQLEN = 1 << 3
+ERR_TIMEOUT = 1 << 4
+ERR_CAND_CAPACITY = 1 << 5
 
 
 class TreeAttnParams(Structure):
@@ -109,6 +111,7 @@ SIGNATURES = {
     "gorgon_abi_version": (c_int, []),
     "gorgon_last_error": (c_char_p, []),
     "gorgon_device_error": (c_int, [POINTER(c_uint32), c_int]),
+    "gorgon_set_wait_limit_ns": (c_int64, [c_int64]),
     "gorgon_tree_mask": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "gorgon_tree_attn_workspace_size": (c_size_t, [POINTER(TreeAttnParams)]),
     "gorgon_tree_attn": (c_int, [POINTER(TreeAttnParams), c_void_p, c_size_t, c_void_p]),
@@ -161,6 +164,12 @@ def device_error(clear: bool = True) -> int:
     flags = c_uint32(0)
     check(lib().gorgon_device_error(ctypes.byref(flags), int(clear)), "gorgon_device_error")
     return int(flags.value)
+
+
+def set_wait_limit_ns(ns: int) -> int:
+    """Sets the bound on every wait inside the tensor-core kernels (process
+    wide, nanoseconds; <= 0 leaves it unchanged) and returns the previous one."""
+    return int(lib().gorgon_set_wait_limit_ns(int(ns)))
 
 
 def pointer_array(ptrs) -> ctypes.Array:

@@ -20,7 +20,7 @@ LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libgorgon_b200.so"
 INCLUDE = PKG.parent / "include"
 
-SOURCES = ["abi.cu", "tree_mask.cu", "attn_api.cu", "attn_simt.cu", "attn_tc.cu",
+SOURCES = ["abi.cu", "tree_mask.cu", "attn_api.cu", "attn_simt.cu", "attn_tc.cu", "attn_pair.cu",
            "verify.cu", "kv_trim.cu", "cand_tree.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

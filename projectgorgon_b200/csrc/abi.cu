@@ -1,5 +1,6 @@
 // Library-wide C ABI pieces: error reporting, the device error word, device
 // properties.  The per-operator entry points live beside their kernels.
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -17,7 +18,10 @@ constexpr int kMaxDevices = 64;
 std::mutex g_dev_mu;
 uint32_t* g_err_addr[kMaxDevices] = {};
 int g_sm_count[kMaxDevices] = {};
+std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
 }  // namespace
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
 
 int set_error(int code, const std::string& msg) {
   g_last_error = msg;
@@ -72,4 +76,11 @@ extern "C" int gorgon_device_error(uint32_t* out_flags, int clear) {
     if (rc) return rc;
   }
   return GORGON_OK;
+}
+
+extern "C" int64_t gorgon_set_wait_limit_ns(int64_t ns) {
+  using namespace gorgon;
+  const uint64_t prev = g_wait_limit_ns.load();
+  if (ns > 0) g_wait_limit_ns.store(static_cast<uint64_t>(ns));
+  return static_cast<int64_t>(prev);
 }

@@ -6,8 +6,6 @@
 
 namespace gorgon {
 
-constexpr uint32_t kErrBadSeqlen = 1u << 3;  // a sequence shorter than its tree
-
 struct AttnArgs {
   const void* q;
   const void* k;
@@ -80,5 +78,9 @@ bool attn_tc_supported(const AttnArgs& a, int dtype);
 int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st);
 size_t attn_tc_workspace(const AttnArgs& a);
 void attn_tc_plan(const AttnArgs& a, int32_t* splits, int32_t* launches);
+// CTA-pair kernel (attn_pair.cu): whole units only, no workspace.
+bool attn_pair_supported(const AttnArgs& a, int dtype);
+int attn_pair_plan(const AttnArgs& a, int dtype, int* pairs, int* units);
+int launch_attn_pair(const AttnArgs& a, int dtype, cudaStream_t st);
 
 }  // namespace gorgon

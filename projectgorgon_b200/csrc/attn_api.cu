@@ -46,8 +46,7 @@ int make_args(const gorgon_tree_attn_params* p, AttnArgs* a) {
     if (p->kv_len == 0 && !p->cu_seqlens)
       return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn: kv_len == 0");
   }
-  if (p->backend != GORGON_BACKEND_AUTO && p->backend != GORGON_BACKEND_SIMT &&
-      p->backend != GORGON_BACKEND_TCGEN05)
+  if (p->backend < GORGON_BACKEND_AUTO || p->backend > GORGON_BACKEND_TCGEN05_CTA)
     return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn: unknown backend");
   if (p->num_splits < 0 || p->num_splits > 1024)
     return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn: num_splits outside [0, 1024]");
@@ -87,12 +86,32 @@ int make_args(const gorgon_tree_attn_params* p, AttnArgs* a) {
   return GORGON_OK;
 }
 
-bool use_tc(const gorgon_tree_attn_params* p, const AttnArgs& a) {
-  if (p->backend == GORGON_BACKEND_SIMT) return false;
-  const bool ok = attn_tc_supported(a, p->dtype);
-  if (p->backend == GORGON_BACKEND_TCGEN05) return ok;
+enum class Kernel { kSimt, kTcCta, kTcPair, kNone };
+
+// The planner does not pick the CTA-pair kernel: measured on B200 it is
+// slower than the single-CTA kernel on every shape tried (16 x 8192 layer
+// 205 us against 144; 2 x 8192 102 against 34), because each of its
+// 128-key tiles puts a 16K-score softmax on four warps and a cross-SM
+// arrival on the critical path.  It stays available as backend
+// GORGON_BACKEND_TCGEN05_PAIR.
+bool pair_preferred(const AttnArgs&, int) { return false; }
+
+Kernel choose(const gorgon_tree_attn_params* p, const AttnArgs& a) {
+  switch (p->backend) {
+    case GORGON_BACKEND_SIMT:
+      return Kernel::kSimt;
+    case GORGON_BACKEND_TCGEN05_PAIR:
+      return attn_pair_supported(a, p->dtype) ? Kernel::kTcPair : Kernel::kNone;
+    case GORGON_BACKEND_TCGEN05_CTA:
+      return attn_tc_supported(a, p->dtype) ? Kernel::kTcCta : Kernel::kNone;
+    default:
+      break;
+  }
+  const bool tc = attn_tc_supported(a, p->dtype);
   // Auto: tensor cores once the packed (group x tree) rows fill an MMA tile.
-  return ok && a.n >= 64;
+  if (p->backend == GORGON_BACKEND_AUTO && !(tc && a.n >= 64)) return Kernel::kSimt;
+  if (!tc) return p->backend == GORGON_BACKEND_TCGEN05 ? Kernel::kNone : Kernel::kSimt;
+  return pair_preferred(a, p->dtype) ? Kernel::kTcPair : Kernel::kTcCta;
 }
 
 int simt_splits(const gorgon_tree_attn_params* p, const AttnArgs& a) {
@@ -121,8 +140,12 @@ extern "C" size_t gorgon_tree_attn_workspace_size(const gorgon_tree_attn_params*
   using namespace gorgon;
   AttnArgs a;
   if (make_args(p, &a) != GORGON_OK) return 0;
-  if (use_tc(p, a)) return attn_tc_workspace(a);
-  return simt_workspace(a, simt_splits(p, a));
+  switch (choose(p, a)) {
+    case Kernel::kTcCta: return attn_tc_workspace(a);
+    case Kernel::kTcPair:
+    case Kernel::kNone: return 0;
+    default: return simt_workspace(a, simt_splits(p, a));
+  }
 }
 
 extern "C" int gorgon_tree_attn_plan(const gorgon_tree_attn_params* p, int32_t* backend,
@@ -132,13 +155,26 @@ extern "C" int gorgon_tree_attn_plan(const gorgon_tree_attn_params* p, int32_t* 
   int rc = make_args(p, &a);
   if (rc) return rc;
   int32_t be, sp, ln;
-  if (use_tc(p, a)) {
-    be = GORGON_BACKEND_TCGEN05;
-    attn_tc_plan(a, &sp, &ln);
-  } else {
-    be = GORGON_BACKEND_SIMT;
-    sp = simt_splits(p, a);
-    ln = sp > 1 ? 2 : 1;
+  switch (choose(p, a)) {
+    case Kernel::kTcCta:
+      be = GORGON_BACKEND_TCGEN05;
+      attn_tc_plan(a, &sp, &ln);
+      break;
+    case Kernel::kTcPair: {
+      int pairs = 0, units = 0;
+      rc = attn_pair_plan(a, p->dtype, &pairs, &units);
+      if (rc) return rc;
+      be = GORGON_BACKEND_TCGEN05_PAIR;
+      sp = 2 * pairs;  // CTAs
+      ln = 1;
+      break;
+    }
+    case Kernel::kNone:
+      return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_tree_attn_plan: the requested tcgen05 kernel does not take this shape");
+    default:
+      be = GORGON_BACKEND_SIMT;
+      sp = simt_splits(p, a);
+      ln = sp > 1 ? 2 : 1;
   }
   if (backend) *backend = be;
   if (splits) *splits = sp;
@@ -154,14 +190,20 @@ extern "C" int gorgon_tree_attn(const gorgon_tree_attn_params* p, void* workspac
   if (rc) return rc;
   if (static_cast<int64_t>(a.batch) * a.hq * a.n * a.d == 0) return GORGON_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (use_tc(p, a)) {
+  const Kernel k = choose(p, a);
+  if (k == Kernel::kTcPair) return launch_attn_pair(a, p->dtype, st);
+  if (k == Kernel::kTcCta) {
     const size_t need = attn_tc_workspace(a);
     if (need > 0 && (!workspace || workspace_bytes < need))
       return set_error(GORGON_ERR_WORKSPACE, "gorgon_tree_attn: workspace smaller than gorgon_tree_attn_workspace_size()");
     return launch_attn_tc(a, p->dtype, workspace, workspace_bytes, st);
   }
-  if (p->backend == GORGON_BACKEND_TCGEN05)
+  if (k == Kernel::kNone) {
+    if (p->backend == GORGON_BACKEND_TCGEN05_PAIR)
+      return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_tree_attn: the tcgen05 pair kernel needs bf16/f16, head_dim 128, a tree mask, "
+                                               "one kv length (no cu_seqlens) and 16-bit output rows of whole 16-byte chunks");
     return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_tree_attn: tcgen05 backend needs bf16/f16, head_dim 128, a tree mask and f32/bf16/f16 output");
+  }
   a.splits = simt_splits(p, a);
   const size_t need = simt_workspace(a, a.splits);
   if (need > 0) {

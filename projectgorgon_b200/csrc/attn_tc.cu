@@ -52,23 +52,16 @@
 
 #include "attn.cuh"
 #include "sm100.cuh"
+#include "attn_tc_common.cuh"
 
 namespace gorgon {
-
-constexpr uint32_t kErrTimeout = 1u << 4;
-
 namespace {
 using namespace sm100;
 
-constexpr int kBM = 128;              // rows per MMA tile
-constexpr int kD = 128;               // head_dim
-constexpr long long kWaitLimitCycles = 4000000000ll;  // about 2 s at the boost clock
-constexpr uint32_t kQHalf = kBM * 128;                 // 128 rows x 64 cols bf16 = 16 KB
 constexpr uint32_t kOffQ = 0;                          // [mtile][half]
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // + (buf * MT + mtile) * BN
 constexpr uint32_t kColO = 256;  // + mtile * 128
-constexpr int kOutBf16 = 1, kOutF16 = 2, kOutF32 = 3;  // TcArgs::out_vec
 
 // The constants that follow from MT, the 128-row M-tiles per CTA.
 template <int MT>
@@ -101,6 +94,7 @@ struct TcArgs {
   float* part_o;      // [grid * 2][rows per unit][128]
   float* part_lse;    // [grid * 2][rows per unit]
   int* tile_start;    // varlen: [units + 1] tile prefix (written by attn_tc_prologue)
+  uint64_t wait_ns;   // bound on every wait (wait_limit_ns())
 };
 
 template <int MT>
@@ -197,79 +191,6 @@ struct Segments {
   }
 };
 
-// Byte offset of 16-byte chunk `c` (0..7) of row `r` in an SW128 K-major
-// tile whose rows are 128 bytes.
-__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) {
-  return r * 128u + ((c ^ (r & 7u)) << 4);
-}
-
-// Packed query row -> (query head within the kv group, tree node), advanced
-// two rows at a time (the rows a half-warp visits in the coalesced Q load and
-// output store).
-struct RowCursor {
-  int pr, gq, node;
-  __device__ __forceinline__ RowCursor(int p, int n) : pr(p), gq(p / n), node(p - (p / n) * n) {}
-  __device__ __forceinline__ void next2(int n) {
-    pr += 2;
-    node += 2;
-    while (node >= n) {  // at most twice: n >= 1
-      node -= n;
-      ++gq;
-    }
-  }
-};
-
-// A softmax warp's 32 rows of its M-tile's Q buffer (two 4 KB pieces, one per
-// d half) double as the warp's staging area for output rows: row rr (0..31)
-// holds 16 chunks of 16 bytes in the same SW128 order as Q, so a thread
-// writing its own row and a half-warp reading one row are both free of bank
-// conflicts.
-__device__ __forceinline__ uint8_t* stage_at(uint8_t* q_tile, int wq, int rr, int j) {
-  return q_tile + (j >> 3) * kQHalf + sw128(static_cast<uint32_t>(wq * 32 + rr), static_cast<uint32_t>(j & 7));
-}
-
-__device__ __forceinline__ uint32_t pack16x2(float x, float y, bool bf16) {
-  if (bf16) {
-    const __nv_bfloat162 v = __floats2bfloat162_rn(x, y);
-    return *reinterpret_cast<const uint32_t*>(&v);
-  }
-  const __half2 v = __floats2half2_rn(x, y);
-  return *reinterpret_cast<const uint32_t*>(&v);
-}
-
-__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  return mbar_wait(bar, parity, abort, kWaitLimitCycles);
-}
-
-// Wait of a thread that does nothing else (the MMA issuers): spins on the
-// non-blocking test so it resumes the moment the phase completes, instead of
-// sleeping in try_wait.  Bounded like bounded_wait.
-__device__ __forceinline__ bool spin_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_test_wait(bar, parity)) return true;
-  long long t0 = 0;
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort) return false;
-      const long long now = clock64();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > kWaitLimitCycles) {
-        *abort = 1;
-        return false;
-      }
-    }
-  }
-}
-
-// Wait used on the way out: ignores the abort flag, gives up after about 100 ms.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > 200000000ll) break;
-  }
-}
-
 // ------------------------------------------------------------ roles
 // Streams one operand (K when is_v == 0, else V) of every tile of the CTA's
 // segments through its ring.
@@ -295,7 +216,7 @@ __device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem,
       const int tile = static_cast<int>(g - pi.start);
       const int stage = static_cast<int>(issued % C::kStages);
       const uint32_t ph = static_cast<uint32_t>(issued / C::kStages) & 1u;
-      if (!bounded_wait(&empty[stage], ph ^ 1u, abort)) {
+      if (!bounded_wait(&empty[stage], ph ^ 1u, abort, t.wait_ns)) {
         ok = false;
         break;
       }
@@ -397,16 +318,16 @@ __device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
   bool ok = true;
   while (ok && sg.next(t, g, e, pi)) {
     const uint32_t n_tiles = static_cast<uint32_t>(e - g);
-    if (!spin_wait(&bars->q_full, seg & 1u, abort)) break;
+    if (!spin_wait(&bars->q_full, seg & 1u, abort, t.wait_ns)) break;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
-      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort)) {
+      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort, t.wait_ns)) {
         ok = false;
         break;
       }
       // per M-tile: each softmax warpgroup starts as soon as its own S lands
       for (int mt = 0; mt < MT && ok; ++mt) {
         const uint32_t bi = (i & 1u) * MT + mt;
-        if (i >= 2 && !spin_wait(&bars->p_free[bi], ((i - 2) >> 1) & 1u, abort)) {
+        if (i >= 2 && !spin_wait(&bars->p_free[bi], ((i - 2) >> 1) & 1u, abort, t.wait_ns)) {
           ok = false;
           break;
         }
@@ -440,13 +361,13 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
     const uint32_t n_tiles = static_cast<uint32_t>(e - g);
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
       const uint32_t buf = i & 1u;
-      if (!spin_wait(&bars->v_full[vr.stage], vr.phase, abort)) {
+      if (!spin_wait(&bars->v_full[vr.stage], vr.phase, abort, t.wait_ns)) {
         ok = false;
         break;
       }
       for (int mt = 0; mt < MT && ok; ++mt) {
         const uint32_t bi = buf * MT + mt;
-        if (!spin_wait(&bars->p_full[bi], (i >> 1) & 1u, abort)) {
+        if (!spin_wait(&bars->p_full[bi], (i >> 1) & 1u, abort, t.wait_ns)) {
           ok = false;
           break;
         }
@@ -463,42 +384,6 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
   drain_wait(&bars->drain[1], 0);
 }
 
-// Visibility of 64 consecutive key columns for one row: bit j is set when
-// column (tree index o + j) is visible -- a prefix column (tree index < 0) or
-// an ancestor of the row's node (bit set in anc).  Built once per masked
-// tile with a funnel shift of the ancestor words, so that masking a column
-// costs a constant-bit test instead of a run-time compare-and-select chain
-// per column (the per-column form made the masked tile the slowest tile of
-// a unit by several microseconds).
-template <int ANCW>
-__device__ __forceinline__ uint64_t vis_window(const uint32_t (&anc)[ANCW], int o) {
-  if (o <= -64) return ~0ull;
-  // word w of the extended bit array: all ones before the tree, 0 after the last word
-  auto word = [&](int w) -> uint32_t {
-    uint32_t r = w < 0 ? 0xffffffffu : 0u;
-#pragma unroll
-    for (int k = 0; k < ANCW; ++k) r = (w == k) ? anc[k] : r;
-    return r;
-  };
-  const int w0 = o >> 5;  // floor(o / 32), also for negative o
-  const int sh = o & 31;
-  const uint64_t lo = static_cast<uint64_t>(word(w0)) | (static_cast<uint64_t>(word(w0 + 1)) << 32);
-  const uint64_t hi = word(w0 + 2);
-  return sh == 0 ? lo : (lo >> sh) | (hi << (64 - sh));
-}
-
-// All 32 lanes wait; the result is the same on every lane.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  const bool ok = bounded_wait(bar, parity, abort);
-  return __all_sync(0xffffffffu, ok);
-}
-
-// Writes 32 finished output columns of one row in any output dtype or layout
-// (the path for rows that are not 16-byte aligned).
-__device__ __forceinline__ void store_cols32(const TcArgs& t, int64_t ob, int col0, const float (&v)[32]) {
-#pragma unroll
-  for (int c = 0; c < 32; ++c) store_as(t.a.out, t.a.out_dtype, ob + col0 + c, v[c]);
-}
 
 template <int MT, int ANCW, bool BF16>
 __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, uint32_t tmem, int64_t g0,
@@ -633,7 +518,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
           vw[2 * hh + 1] = static_cast<uint32_t>(w >> 32);
         }
       }
-      if (!warp_wait(&bars->s_full[bi], static_cast<uint32_t>(i >> 1) & 1u, abort)) return false;
+      if (!warp_wait(&bars->s_full[bi], static_cast<uint32_t>(i >> 1) & 1u, abort, t.wait_ns)) return false;
       tc_fence_after();
       const uint32_t s_addr = lane_base + kColS + bi * kBN;
       float x[kBN];
@@ -697,7 +582,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
-        if (!warp_wait(&bars->p_free[(pv & 1) * MT + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort))
+        if (!warp_wait(&bars->p_free[(pv & 1) * MT + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort, t.wait_ns))
           return false;
         tc_fence_after();
         const uint32_t o_addr = lane_base + kColO + wg * kD;
@@ -735,7 +620,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
 
     // ---- epilogue: O / l for this row, once the last P.V has landed
     const int64_t lastv = i - 1;
-    if (!warp_wait(&bars->p_free[(lastv & 1) * MT + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort)) return;
+    if (!warp_wait(&bars->p_free[(lastv & 1) * MT + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort, t.wait_ns)) return;
     tc_fence_after();
     const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
     const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
@@ -829,7 +714,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
         float vals[32];
 #pragma unroll
         for (int c = 0; c < 32; ++c) vals[c] = __uint_as_float(ov[c]) * inv;
-        if (row_ok) store_cols32(t, ob, ch * 32, vals);
+        if (row_ok) store_cols32(t.a, ob, ch * 32, vals);
       }
     }
     if (whole) {
@@ -1315,6 +1200,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.grid = pl.grid;
   t.pair_align = pl.pair_align;
   t.ab_fmt = dtype == GORGON_BF16 ? 1 : 0;
+  t.wait_ns = wait_limit_ns();
   char* ws = static_cast<char*>(workspace);
   t.tile_start = reinterpret_cast<int*>(ws + w.tile_start);
   t.part_lse = reinterpret_cast<float*>(ws + w.part_lse);

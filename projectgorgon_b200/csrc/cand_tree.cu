@@ -41,7 +41,6 @@
 
 namespace gorgon {
 
-constexpr uint32_t kErrCandCapacity = 1u << 3;
 
 namespace {
 using namespace sm100;

@@ -17,6 +17,9 @@ namespace gorgon {
 constexpr uint32_t kErrBadParent = 1u << 0;
 constexpr uint32_t kErrBadTrimIndex = 1u << 1;
 constexpr uint32_t kErrBadVerifyInput = 1u << 2;
+constexpr uint32_t kErrBadSeqlen = 1u << 3;      // a sequence shorter than its tree
+constexpr uint32_t kErrTimeout = 1u << 4;        // a bounded wait of a tensor-core kernel ran out
+constexpr uint32_t kErrCandCapacity = 1u << 5;   // a candidate tree was cut at max_nodes
 
 // Sets the calling thread's last-error message and returns `code`.
 int set_error(int code, const std::string& msg);
@@ -26,6 +29,9 @@ int check_cuda(cudaError_t e, const char* what);
 uint32_t* device_error_word();
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// Bound, in nanoseconds, on every wait inside the tensor-core kernels
+// (2 s unless changed through gorgon_set_wait_limit_ns).
+uint64_t wait_limit_ns();
 
 __device__ __forceinline__ void raise_device_error(uint32_t* word, uint32_t bit) {
   if (word) atomicOr(word, bit);

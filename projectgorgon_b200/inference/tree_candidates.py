@@ -138,7 +138,7 @@ def build_candidate_trees(logits: torch.Tensor, top_k: int = 4, max_candidates: 
     sequence's ``[L, V]``), level ``l + 1`` from head ``l``.  The rules are
     ``build_candidate_tree``'s; ``max_nodes`` (default: the largest tree the
     rules allow) is the capacity per row, at most 4096 -- a tree cut there
-    sets device error bit 3."""
+    sets device error bit 5."""
     lg = _logits3(logits)
     B, L, V = lg.shape
     cap = max_nodes if max_nodes is not None else max_tree_nodes(top_k, L, V, max_candidates)

@@ -26,7 +26,8 @@ import torch
 from .. import _abi
 from .._util import gorgon_dtype, on_device, parents_tensor, ptr, require_cuda, stream_ptr, workspace
 
-_BACKENDS = {"auto": _abi.BACKEND_AUTO, "simt": _abi.BACKEND_SIMT, "tcgen05": _abi.BACKEND_TCGEN05}
+_BACKENDS = {"auto": _abi.BACKEND_AUTO, "simt": _abi.BACKEND_SIMT, "tcgen05": _abi.BACKEND_TCGEN05,
+             "tcgen05-pair": _abi.BACKEND_TCGEN05_PAIR, "tcgen05-cta": _abi.BACKEND_TCGEN05_CTA}
 
 
 def _as4(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -87,8 +88,12 @@ def tree_attention(
 
 def tree_attention_plan(q, k, v, tree_mask=None, **kwargs) -> dict:
     """The launch plan ``tree_attention`` would use for these arguments:
-    ``backend`` ("simt" or "tcgen05"), ``splits``, ``launches`` (kernels per
-    call) and ``workspace_bytes``."""
+    ``backend`` ("simt", "tcgen05" for the single-CTA tensor-core kernel or
+    "tcgen05-pair" for the CTA-pair one), ``splits`` (CTAs of the tensor-core
+    grid, or the CUDA-core kernel's key splits), ``launches`` (kernels per
+    call) and ``workspace_bytes``.  ``backend=`` in the arguments requests one
+    ("auto", "simt", "tcgen05" -- either tensor-core shape, the planner's
+    pick -- "tcgen05-pair" or "tcgen05-cta")."""
     args = dict(parents=None, max_depth=None, cu_seqlens=None, max_seqlen=None, scale=None,
                 out_dtype=None, return_lse=False, backend="auto", num_splits=0)
     args.update(kwargs)
@@ -101,7 +106,7 @@ def tree_attention_plan(q, k, v, tree_mask=None, **kwargs) -> dict:
         _abi.check(lib.gorgon_tree_attn_plan(prep.p, ctypes.byref(be), ctypes.byref(sp), ctypes.byref(ln)),
                    "gorgon_tree_attn_plan")
         nbytes = lib.gorgon_tree_attn_workspace_size(prep.p)
-    names = {_abi.BACKEND_SIMT: "simt", _abi.BACKEND_TCGEN05: "tcgen05"}
+    names = {_abi.BACKEND_SIMT: "simt", _abi.BACKEND_TCGEN05: "tcgen05", _abi.BACKEND_TCGEN05_PAIR: "tcgen05-pair"}
     return {"backend": names.get(be.value, str(be.value)), "splits": sp.value, "launches": ln.value,
             "workspace_bytes": int(nbytes)}
 

@@ -116,3 +116,15 @@ def test_empty_problems_are_no_ops():
     t = _abi.KvTrimParams()
     t.elem_bytes = 2
     assert lib.gorgon_kv_trim(t, None) == 0
+
+
+def test_wait_limit_setter_round_trips():
+    """gorgon_set_wait_limit_ns returns the previous bound; ns <= 0 changes nothing."""
+    first = _abi.set_wait_limit_ns(123456)
+    try:
+        assert first > 0
+        assert _abi.set_wait_limit_ns(0) == 123456
+        assert _abi.set_wait_limit_ns(-5) == 123456
+    finally:
+        _abi.set_wait_limit_ns(first)
+    assert _abi.set_wait_limit_ns(0) == first

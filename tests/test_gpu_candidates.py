@@ -9,6 +9,7 @@ import pytest
 import torch
 
 import projectgorgon_b200 as G
+from projectgorgon_b200 import _abi
 from conftest import load_golden
 from oracle import gorgon_oracle as O
 from projectgorgon_b200.inference import build_candidate_trees, head_statistics, max_tree_nodes
@@ -149,7 +150,7 @@ def test_capacity_cut_sets_error_bit():
     lg = torch.randn(2, 3, 500, device="cuda", generator=g)
     trees = build_candidate_trees(lg, top_k=4, max_nodes=30)
     torch.cuda.synchronize()
-    assert G.device_error(clear=True) & 8
+    assert G.device_error(clear=True) & _abi.ERR_CAND_CAPACITY
     full = _oracle_trees(lg.cpu().numpy(), 4)
     for b in range(2):
         assert int(trees.n_nodes[b]) == 30
