@@ -77,6 +77,12 @@ struct Cfg {
   static constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
   static constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;  // + alignment slack
+  // Who frees a K stage: with two M-tiles (a 5-stage ring) each softmax
+  // warpgroup arrives once it has seen its S, which takes a barrier
+  // operation off the Q.K^T issuer, the busiest thread; with one M-tile
+  // (a 3-stage ring) the issuer commits the release as soon as its MMAs
+  // complete, so the shorter ring refills sooner.
+  static constexpr bool kSoftmaxFreesK = MT == 2;
   static_assert(kSmemBytes <= 232448, "shared memory per block");
   static_assert(2 * MT * kBN <= kColO, "S buffers below O");
 };
@@ -107,7 +113,7 @@ struct Barriers {
   // per (S buffer, M-tile): index buf * MT + mtile
   uint64_t s_full[2 * MT];
   uint64_t p_full[2 * MT];
-  uint64_t p_free[2 * MT];  // P.V of the tile in this buffer has completed
+  uint64_t p_free[2];       // P.V of every M-tile of the tile in this buffer has completed
   uint64_t drain[2];        // all MMAs of the Q.K^T / P.V issuer complete
   uint32_t tmem_base;
   int abort;
@@ -320,23 +326,26 @@ __device__ void qk_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
     const uint32_t n_tiles = static_cast<uint32_t>(e - g);
     if (!spin_wait(&bars->q_full, seg & 1u, abort, t.wait_ns)) break;
     for (uint32_t j = 0; j < n_tiles; ++j, ++i) {
-      if (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort, t.wait_ns)) {
+      // Both probes are issued before either result is used, so when the K
+      // tile and the S buffer are already there (the usual case) the two
+      // barrier round trips overlap; otherwise fall back to bounded spins.
+      const uint32_t pf_par = ((i - 2) >> 1) & 1u;
+      const bool k_ready = mbar_test_wait(&bars->k_full[kr.stage], kr.phase);
+      const bool p_ready = i < 2 || mbar_test_wait(&bars->p_free[i & 1u], pf_par);
+      if (!(k_ready && p_ready) &&
+          (!spin_wait(&bars->k_full[kr.stage], kr.phase, abort, t.wait_ns) ||
+           (i >= 2 && !spin_wait(&bars->p_free[i & 1u], pf_par, abort, t.wait_ns)))) {
         ok = false;
         break;
       }
+      tc_fence_after();
       // per M-tile: each softmax warpgroup starts as soon as its own S lands
-      for (int mt = 0; mt < MT && ok; ++mt) {
-        const uint32_t bi = (i & 1u) * MT + mt;
-        if (i >= 2 && !spin_wait(&bars->p_free[bi], ((i - 2) >> 1) & 1u, abort, t.wait_ns)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
         issue_qk<MT>(md, tmem, kr.stage, i & 1u, mt);
-        umma_commit(&bars->s_full[bi]);
+        umma_commit(&bars->s_full[(i & 1u) * MT + mt]);
       }
-      if (!ok) break;
-      umma_commit(&bars->k_empty[kr.stage]);
+      if (!Cfg<MT>::kSoftmaxFreesK) umma_commit(&bars->k_empty[kr.stage]);
       kr.next();
     }
     ++seg;
@@ -373,9 +382,9 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
         }
         tc_fence_after();
         issue_pv<MT>(md, tmem, vr.stage, buf, mt, j == 0);
-        umma_commit(&bars->p_free[bi]);
       }
       if (!ok) break;
+      umma_commit(&bars->p_free[buf]);
       umma_commit(&bars->v_empty[vr.stage]);
       vr.next();
     }
@@ -519,6 +528,9 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
         }
       }
       if (!warp_wait(&bars->s_full[bi], static_cast<uint32_t>(i >> 1) & 1u, abort, t.wait_ns)) return false;
+      // this M-tile's Q.K^T of the tile has completed: the K stage is free
+      // once every warpgroup has seen its S (kSoftmaxFreesK)
+      if (C::kSoftmaxFreesK && wq == 0 && lane == 0) mbar_arrive(&bars->k_empty[static_cast<uint32_t>(i % C::kStages)]);
       tc_fence_after();
       const uint32_t s_addr = lane_base + kColS + bi * kBN;
       float x[kBN];
@@ -582,7 +594,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
       // rescale O (warp-uniform) once the P.V of tile i - 1 has landed
       if (__any_sync(0xffffffffu, need)) {
         const int64_t pv = i - 1;
-        if (!warp_wait(&bars->p_free[(pv & 1) * MT + wg], static_cast<uint32_t>(pv >> 1) & 1u, abort, t.wait_ns))
+        if (!warp_wait(&bars->p_free[pv & 1], static_cast<uint32_t>(pv >> 1) & 1u, abort, t.wait_ns))
           return false;
         tc_fence_after();
         const uint32_t o_addr = lane_base + kColO + wg * kD;
@@ -620,7 +632,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
 
     // ---- epilogue: O / l for this row, once the last P.V has landed
     const int64_t lastv = i - 1;
-    if (!warp_wait(&bars->p_free[(lastv & 1) * MT + wg], static_cast<uint32_t>(lastv >> 1) & 1u, abort, t.wait_ns)) return;
+    if (!warp_wait(&bars->p_free[lastv & 1], static_cast<uint32_t>(lastv >> 1) & 1u, abort, t.wait_ns)) return;
     tc_fence_after();
     const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
     const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
@@ -739,7 +751,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&bars->k_full[s], 1);
-      mbar_init(&bars->k_empty[s], 1);
+      mbar_init(&bars->k_empty[s], C::kSoftmaxFreesK ? MT : 1);
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
@@ -747,8 +759,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     for (int b = 0; b < 2 * MT; ++b) {
       mbar_init(&bars->s_full[b], 1);
       mbar_init(&bars->p_full[b], 4);  // the four warps of one softmax warpgroup
-      mbar_init(&bars->p_free[b], 1);
     }
+    mbar_init(&bars->p_free[0], 1);
+    mbar_init(&bars->p_free[1], 1);
     mbar_init(&bars->drain[0], 1);
     mbar_init(&bars->drain[1], 1);
     bars->abort = 0;
