@@ -879,12 +879,12 @@ class ClockSampler:
             log(f"clock sampling unavailable: {exc}")
         return self
 
-    def poll(self):
-        """One sample from the calling thread (the timing loop calls it right
-        after launching a step, while the GPU still has queued work), at most
-        one per sampling period so the launches stay ahead of the GPU."""
+    def poll(self, force: bool = False):
+        """One sample from the calling thread, at most one per sampling period
+        unless `force` (the timing loop samples after it has queued every
+        step, while the GPU works through them)."""
         now = time.perf_counter()
-        if self._sample is not None and now - self._last_poll >= self.period:
+        if self._sample is not None and (force or now - self._last_poll >= self.period):
             self._last_poll = now
             self._sample()
 
@@ -936,6 +936,7 @@ def cpu_baseline(wl: "Workload", budget_s: float = 12.0):
     ha.run_seq(0)  # warm-up
     done, secs, nbytes = 0, 0.0, 0
     while done < wl.cfg["B"] and (done == 0 or secs < budget_s):
+        ha.seq_inputs(done)  # drawn outside the timed call
         t0 = time.perf_counter()
         ha.run_seq(done)
         secs += time.perf_counter() - t0
@@ -984,7 +985,12 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
             starts[i].record(st)
             wl.step()
             ends[i].record(st)
-            clk.poll()
+        # every step is queued: sample the clocks while the GPU works through
+        # them (an NVML read takes about a millisecond, so reading between
+        # launches would leave the GPU waiting for the next one)
+        clk.poll(force=True)
+        while not ends[-1].query():
+            clk.poll(force=True)
         torch.cuda.synchronize(dev)
     total_ms = starts[0].elapsed_time(ends[-1])
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
