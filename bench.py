@@ -48,8 +48,8 @@ from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tre
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
 NCU_TRAFFIC_BYTES = {
-    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.552 MB read + 3.763 MB written
-    ("verify-b16-p8192-n64", "tcgen05"): 553314560,
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.551 MB read + 4.671 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 554221568,
     # profiles/attn_tc_kernel_verify-b1-p2048-n64.md: 9.273 MB read, 0 written
     ("verify-b1-p2048-n64", "tcgen05"): 9273088,
     # profiles/verify_kernel_verifier-b32-n64-v128256.md: 570.646 MB read + 4.049 MB written
