@@ -283,6 +283,7 @@ class Workload:
         return self.cfg.get("bound", "hbm")
 
     mode = "strong"
+    graphable = True  # one step is one stream-ordered public call
 
     def config(self, world: int, plan: dict) -> dict:
         return attn_config(self.name, world, self.mode)
@@ -372,6 +373,7 @@ class HeadShardWorkload(Workload):
         return sharding.gather_heads(o)
 
     mode = "heads"
+    graphable = False  # the step holds an NCCL all-gather: timed eagerly
 
     def extra(self, world: int, ms_step: float) -> dict:
         ev = self.kernel_events[-min(len(self.kernel_events), 50):]
@@ -962,16 +964,48 @@ def dist_setup():
     return env.world, env.rank, env.local_rank
 
 
-def time_device(wl: Workload, steps: int, warmup: int, world: int):
+def capture_step(wl, dev):
+    """A CUDA graph of one step (the public call, captured once on a side
+    stream as torch requires), replayed for each timed step: the way a
+    serving loop runs a launch-bound step, without the per-call host path
+    and driver launch cost in the device time."""
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            wl.step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        wl.step()
+    return g
+
+
+def time_device(wl: Workload, steps: int, warmup: int, world: int, graph: bool = False):
     """(ms of the timed steps, mean ms per step, clock summary).  A workload
     whose inputs fit in L2 sets ``flush_l2``: a 256 MB write then evicts L2
     before every step, outside the step's events, and the time is the sum of
-    the steps' own event times."""
+    the steps' own event times.  With `graph`, each step replays a CUDA graph
+    of the step (see capture_step); the warm-up steps run eagerly first."""
     dev = wl.dev
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if getattr(wl, "flush_l2", False) else None
     for _ in range(warmup):
         wl.step()
     torch.cuda.synchronize(dev)
+    step = wl.step
+    g = None
+    if graph:
+        try:
+            g = capture_step(wl, dev)
+        except RuntimeError as exc:  # a capture the runtime refuses: time eager calls instead
+            log(f"CUDA-graph capture failed ({exc}); timing eager calls")
+            wl.graph_failed = True
+        if g is not None:
+            step = g.replay
+            for _ in range(2):
+                step()
+        torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
@@ -983,7 +1017,7 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
             if flush is not None:
                 flush.fill_(i & 0xff)
             starts[i].record(st)
-            wl.step()
+            step()
             ends[i].record(st)
         # every step is queued: sample the clocks while the GPU works through
         # them (an NVML read takes about a millisecond, so reading between
@@ -996,6 +1030,7 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int):
     per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     if flush is not None:
         total_ms = float(np.sum(per))
+    del g
     if world > 1:
         torch.distributed.barrier()
     return total_ms, float(np.mean(per)), clk.summary()
@@ -1196,7 +1231,8 @@ def run_ours(args):
     plan = wl.plan()
     # bytes of the whole job: every rank's share (weak: every rank's batch)
     job_bytes = int(sharding.sum_over_ranks(wl.bytes, dev)) if world > 1 else wl.bytes
-    total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world)
+    graph = not args.eager and getattr(wl, "graphable", False)
+    total_ms, launch_ms, clocks = time_device(wl, args.steps, args.warmup, world, graph=graph)
     total_ms = max_over_ranks(total_ms, world, dev)
     launch_ms = max_over_ranks(launch_ms, world, dev)
     e2e_steps = args.e2e_steps or max(100, args.steps)
@@ -1251,7 +1287,9 @@ def run_ours(args):
         "dtype": wl.cfg["dtype"],
         "data": wl.data,
         "config": wl.config(world, plan),
-        "plan": {"backend": plan["backend"], "splits": plan.get("splits"), "launches_per_step": plan["launches"]},
+        "plan": {"backend": plan["backend"], "splits": plan.get("splits"), "launches_per_step": plan["launches"],
+                 "timed_as": ("CUDA graph of one step, replayed per step"
+                              if graph and not getattr(wl, "graph_failed", False) else "eager public call per step")},
         "pct_of_8tbs": round(100.0 * value / world / 8000.0, 2),
         "roofline": roof,
         "e2e": e2e_out,
@@ -1509,6 +1547,8 @@ def main():
                          "scaling, default), a whole batch per rank (weak scaling), or one layer's kv heads "
                          "per rank with an NCCL all-gather of the output (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager public calls per step instead of replaying a CUDA graph of the step")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()
     if args.warmup < 3:
