@@ -319,10 +319,13 @@ class HeadShardWorkload(Workload):
 
     scaling = "strong"
 
-    def __init__(self, name: str, dev: torch.device, rank: int, world: int):
+    def __init__(self, name: str, dev: torch.device, rank: int, world: int, chunks: int = 1):
         cfg = WORKLOADS[name]
         if isinstance(cfg["P"], tuple):
             raise SystemExit("--shard heads needs a workload with one prefix length")
+        if cfg["B"] % chunks:
+            raise SystemExit(f"--head-chunks {chunks} does not divide the batch of {cfg['B']}")
+        self.chunks = chunks
         self.name, self.cfg, self.dev = name, cfg, dev
         B, Hq, Hkv, D, N, P = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"], cfg["P"]
         (h0, h1), (q0, q1) = sharding.shard_heads(Hkv, Hq, world, rank)
@@ -348,10 +351,16 @@ class HeadShardWorkload(Workload):
                 self.k[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
                 self.v[j, h - h0] = (torch.randn(L, D, device=dev, generator=g) * s).to(dt)
         self.par_t = torch.tensor(self.parents, dtype=torch.int32, device=dev)
-        # the layer output, head-major: this rank's heads are one contiguous
-        # chunk that the attention writes and the in-place all-gather sends
-        self.full, self.local = sharding.head_sharded_output(B, Hq, N, D, dt, dev, world, rank)
-        self.out = self.full.permute(1, 0, 2, 3)
+        # the layer output, head-major per batch chunk: this rank's heads are
+        # one contiguous piece of each chunk's buffer, which the attention
+        # writes and the in-place all-gather sends; chunk c's gather runs on
+        # NCCL's stream while chunk c + 1's attention computes
+        Bc = B // chunks
+        bufs = [sharding.head_sharded_output(Bc, Hq, N, D, dt, dev, world, rank) for _ in range(chunks)]
+        self.fulls = [f for f, _ in bufs]
+        self.locals = [l for _, l in bufs]
+        self.full, self.local = bufs[0]
+        self.out = torch.empty(B, Hq, N, D, device=dev, dtype=dt)  # shape only (the e2e copy-out buffer)
         esz = torch.tensor([], dtype=dt).element_size()
         # this rank's share: its K/V, Q and output slice, and the parents
         self.bytes = 2 * B * (h1 - h0) * L * D * esz + 2 * B * (q1 - q0) * N * D * esz + B * N * 4
@@ -362,11 +371,28 @@ class HeadShardWorkload(Workload):
     def step(self):
         st = torch.cuda.current_stream(self.dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if self.chunks == 1:
+            e0.record(st)
+            G.fused_tree_verify(self.q, self.k, self.v, out=self.local, **self.kwargs())
+            e1.record(st)
+            self.kernel_events.append((e0, e1))
+            return sharding.gather_heads_inplace(self.full)
+        Bc = self.q.shape[0] // self.chunks
+        works, views = [], []
         e0.record(st)
-        G.fused_tree_verify(self.q, self.k, self.v, out=self.local, **self.kwargs())
-        e1.record(st)
+        for c in range(self.chunks):
+            sl = slice(c * Bc, (c + 1) * Bc)
+            G.fused_tree_verify(self.q[sl], self.k[sl], self.v[sl], self.par_t[sl], max_depth=self.max_depth,
+                                out=self.locals[c])
+            view, work = sharding.gather_heads_inplace(self.fulls[c], async_op=True)
+            views.append(view)
+            works.append(work)
+        e1.record(st)  # all attention chunks queued (the gathers overlap them on NCCL's stream)
         self.kernel_events.append((e0, e1))
-        return sharding.gather_heads_inplace(self.full)
+        for w in works:
+            if w is not None:
+                w.wait()
+        return views
 
     def post(self, o):
         """The output gather of one e2e step (a fresh buffer per step)."""
@@ -376,7 +402,7 @@ class HeadShardWorkload(Workload):
     graphable = False  # the step holds an NCCL all-gather: timed eagerly
 
     def extra(self, world: int, ms_step: float) -> dict:
-        ev = self.kernel_events[-min(len(self.kernel_events), 50):]
+        ev = self.kernel_events
         torch.cuda.synchronize(self.dev)
         k_ms = float(np.mean([a.elapsed_time(b) for a, b in ev])) if ev else float("nan")
         return {"us_per_layer": round(ms_step * 1e3, 2), "kernel_only_us": round(k_ms * 1e3, 2),
@@ -874,6 +900,11 @@ class ClockSampler:
                     sample()
                     self._stop.wait(self.period)
 
+            # the first reads of a process take milliseconds (measured: up to
+            # 5 ms, then about 1 us each): made here, outside the timed region
+            for _ in range(3):
+                sample()
+            self.samples.clear()
             self._sample = sample
             self._thread = threading.Thread(target=run, daemon=True)
             self._thread.start()
@@ -993,6 +1024,8 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int, graph: bool =
     for _ in range(warmup):
         wl.step()
     torch.cuda.synchronize(dev)
+    if hasattr(wl, "kernel_events"):
+        wl.kernel_events.clear()  # only the timed steps' attention events count
     step = wl.step
     g = None
     if graph:
@@ -1020,8 +1053,8 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int, graph: bool =
             step()
             ends[i].record(st)
         # every step is queued: sample the clocks while the GPU works through
-        # them (an NVML read takes about a millisecond, so reading between
-        # launches would leave the GPU waiting for the next one)
+        # them (a read takes about a microsecond, but an occasional one takes
+        # milliseconds, which between launches would leave the GPU waiting)
         clk.poll(force=True)
         while not ends[-1].query():
             clk.poll(force=True)
@@ -1217,7 +1250,7 @@ def run_ours(args):
     if args.shard == "heads":
         if kind != "attn":
             raise SystemExit("--shard heads applies to the attention workloads")
-        wl = HeadShardWorkload(args.workload, dev, rank, world)
+        wl = HeadShardWorkload(args.workload, dev, rank, world, chunks=args.head_chunks)
     elif kind == "attn":
         # strong (default): the fixed batch split over the ranks; weak: a batch per rank
         mode = "weak" if args.shard == "weak" else "strong"
@@ -1547,6 +1580,8 @@ def main():
                          "scaling, default), a whole batch per rank (weak scaling), or one layer's kv heads "
                          "per rank with an NCCL all-gather of the output (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--head-chunks", type=int, default=1,
+                    help="--shard heads: batch chunks whose all-gathers overlap the next chunk's attention")
     ap.add_argument("--eager", action="store_true",
                     help="time eager public calls per step instead of replaying a CUDA graph of the step")
     ap.add_argument("--cpu-budget", type=float, default=12.0)

@@ -43,8 +43,9 @@
 //
 // Every wait is bounded (wait_limit_ns()); a CTA whose wait runs out sets
 // its own and its partner's abort flag, so both stop, drain what they
-// issued, free TMEM and raise kErrTimeout.  Whole units only: the planner
-// uses this kernel when the units spread evenly over the GPU's CTA pairs.
+// issued, free TMEM and raise kErrTimeout.  Whole units only.  It runs when
+// asked for (backend GORGON_BACKEND_TCGEN05_PAIR): measured on B200 it is
+// slower than the single-CTA kernel, so the planner does not pick it.
 #include <cuda.h>
 
 #include <mutex>

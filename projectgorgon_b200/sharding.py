@@ -131,21 +131,26 @@ def head_sharded_output(batch: int, heads_q: int, n: int, d: int, dtype: torch.d
     return full, full[rank * per:(rank + 1) * per].permute(1, 0, 2, 3)
 
 
-def gather_heads_inplace(full: torch.Tensor) -> torch.Tensor:
+def gather_heads_inplace(full: torch.Tensor, async_op: bool = False):
     """All-gathers a head-major output (:func:`head_sharded_output`) in place:
     rank r's chunk is the send buffer and the whole buffer the receive buffer
     (NCCL's in-place all-gather), so every rank ends with the layer's output.
-    Returns it as ``[B, Hq, N, D]`` (a view with head-major strides)."""
+    Returns it as ``[B, Hq, N, D]`` (a view with head-major strides); with
+    ``async_op`` returns ``(view, work)``, the gather running on NCCL's stream
+    once the work queued so far on the current stream is done, so the caller
+    can queue more compute before ``work.wait()``."""
+    work = None
     if dist.is_initialized() and dist.get_world_size() > 1:
         world, rank = dist.get_world_size(), dist.get_rank()
         flat = full.view(-1)
         chunk = flat.numel() // world
         mine = flat[rank * chunk:(rank + 1) * chunk]
         if dist.get_backend() == "nccl":
-            dist.all_gather_into_tensor(flat, mine)
+            work = dist.all_gather_into_tensor(flat, mine, async_op=async_op)
         else:
-            dist.all_gather(list(flat.view(world, chunk).unbind(0)), mine.clone())
-    return full.permute(1, 0, 2, 3)
+            work = dist.all_gather(list(flat.view(world, chunk).unbind(0)), mine.clone(), async_op=async_op)
+    view = full.permute(1, 0, 2, 3)
+    return (view, work) if async_op else view
 
 
 def max_over_ranks(value: float, device: torch.device = None) -> float:

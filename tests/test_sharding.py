@@ -83,6 +83,12 @@ def _rank_main(rank, world, port, q):
         assert local.shape == (3, 4, 5, 2)
         local.copy_(o[:, q0:q1])
         ok = ok and bool(torch.equal(sharding.gather_heads_inplace(hm), o))
+        # the asynchronous form: the view is complete once the work is waited on
+        hm2, local2 = sharding.head_sharded_output(3, 8, 5, 2, torch.float32, torch.device("cpu"), world, rank)
+        local2.copy_(o[:, q0:q1])
+        view, work = sharding.gather_heads_inplace(hm2, async_op=True)
+        work.wait()
+        ok = ok and bool(torch.equal(view, o))
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
         q.put((rank, t, ok))
