@@ -17,11 +17,16 @@
 //
 // Schedule: a grid of at most one CTA per SM.  When whole units roughly fill
 // the SMs, CTA c takes units c, c + grid, ... (so the units that share K/V run
-// at the same time).  Otherwise (stream-K) the unit-major list of K/V tiles
-// is split into equal contiguous ranges: a unit that falls inside one CTA is
-// finished there; a unit cut between CTAs leaves normalised partials plus
-// log-sum-exp in the workspace, and attn_tc_combine, launched right after,
-// merges them with one warp per row.
+// at the same time).  With room for two or more CTAs per unit (uniform
+// lengths), each unit is cut into equal tile ranges over the CTAs of one
+// thread-block cluster: every piece leaves its normalised rows and
+// log-sum-exp in its own shared memory, and after a cluster barrier each CTA
+// merges a slice of the unit's rows by reading all pieces through
+// distributed shared memory (one launch, no workspace).  Otherwise (stream-K)
+// the unit-major list of K/V tiles is split into equal contiguous ranges: a
+// unit that falls inside one CTA is finished there; a unit cut between CTAs
+// leaves normalised partials plus log-sum-exp in the workspace, and
+// attn_tc_combine, launched right after, merges them with one warp per row.
 //
 // Warp roles:
 //   warp 0       TMA producer for K tiles (two 64-column SW128 boxes)
@@ -45,6 +50,7 @@
 // and returns.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 #include <type_traits>
 #include <utility>
@@ -84,6 +90,8 @@ struct Cfg {
   // complete, so the shorter ring refills sooner.
   static constexpr bool kSoftmaxFreesK = MT == 2;
   static_assert(kSmemBytes <= 232448, "shared memory per block");
+  // a cluster piece's fp32 rows and log-sum-exp fit in the idle K and V rings
+  static_assert(kQRows * (kD * 4 + 4) <= 2 * kStages * kTileBytes, "cluster partials");
   static_assert(2 * MT * kBN <= kColO, "S buffers below O");
 };
 
@@ -95,6 +103,7 @@ struct TcArgs {
   int tiles_per_pair; // tiles per unit (uniform lengths only)
   int grid;
   int pair_align;     // whole units per CTA, strided by the grid (no partials to merge)
+  int cluster;        // > 1: each unit cut between the CTAs of a cluster of this size, merged in DSMEM
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // 16-byte aligned output rows: kOutBf16 / kOutF16 / kOutF32, else 0
   float* part_o;      // [grid * 2][rows per unit][128]
@@ -416,7 +425,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
   int64_t g, e;
   PairInfo pi;
   while (sg.next(t, g, e, pi)) {
-    const bool whole = g == pi.start && e == pi.end;
+    const bool whole = !t.cluster && g == pi.start && e == pi.end;
     const int64_t i_first = i;
     const int pr = pi.qg * C::kQRows + qrow;  // packed row
     const bool row_ok = pr < R;
@@ -650,6 +659,31 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     const int mode = whole ? t.out_vec : kOutF32;
     const float inv = 1.f / l;  // whole, l == 0: no visible key, NaN like softmax
     const bool zero = !whole && !(l > 0.f);
+    if (t.cluster) {
+      // A piece of a unit cut between the CTAs of a cluster: the normalised
+      // row (0 where nothing was visible) and its log-sum-exp stay in this
+      // CTA's shared memory (the K and V rings, idle once the last P.V has
+      // completed), where cluster_merge reads them.  16-byte chunk j of row q
+      // sits at chunk j ^ (q & 7), so both a warp's row-per-thread stores and
+      // the merge's row-per-warp loads use every bank.
+      uint8_t* prow = smem + C::kOffK + static_cast<uint32_t>(qrow) * (kD * 4);
+#pragma unroll
+      for (int ch = 0; ch < kD / 32; ++ch) {
+        uint32_t ov[32];
+        tmem_ld32(o_addr + ch * 32, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = ch * 8 + u;
+          *reinterpret_cast<float4*>(prow + ((j ^ (qrow & 7)) << 4)) =
+              zero ? make_float4(0.f, 0.f, 0.f, 0.f)
+                   : make_float4(__uint_as_float(ov[4 * u]) * inv, __uint_as_float(ov[4 * u + 1]) * inv,
+                                 __uint_as_float(ov[4 * u + 2]) * inv, __uint_as_float(ov[4 * u + 3]) * inv);
+        }
+      }
+      reinterpret_cast<float*>(smem + C::kOffK + C::kQRows * (kD * 4))[qrow] = lse2;
+      continue;
+    }
     if (mode == kOutBf16 || mode == kOutF16) {
 #pragma unroll
       for (int ch = 0; ch < kD / 32; ++ch) {
@@ -737,6 +771,9 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
   }
 }
 
+template <int MT>
+__device__ void cluster_merge(const TcArgs& t, uint8_t* smem);
+
 template <int MT, int ANCW, bool BF16>
 __global__ void __launch_bounds__(Cfg<MT>::kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
@@ -784,6 +821,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   bool work;
   if (t.pair_align) {
     work = static_cast<int>(blockIdx.x) < t.pairs;
+  } else if (t.cluster) {
+    // unit blockIdx.x / cluster, cut into equal tile ranges, one per CTA of its cluster
+    const int c = static_cast<int>(blockIdx.x) % t.cluster;
+    const PairInfo pu = pair_info(t, static_cast<int>(blockIdx.x) / t.cluster);
+    const int64_t n = pu.end - pu.start;
+    g0 = pu.start + n * c / t.cluster;
+    g1 = pu.start + n * (c + 1) / t.cluster;
+    work = g0 < g1;
   } else {
     const int64_t T = total_tiles(t);
     g0 = range_start(blockIdx.x, T, t.grid);
@@ -807,6 +852,19 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   __syncwarp();  // role warps ran their loop on lane 0: reconverge before the CTA barrier
   tc_fence_before();
   __syncthreads();
+  if (t.cluster) {
+    // Every thread of every CTA of the cluster passes both barriers (the roles
+    // return here on every path, a timeout included).
+    if (!work) {  // a piece with no tiles contributes nothing
+      float* lse_s = reinterpret_cast<float*>(smem + C::kOffK + C::kQRows * (kD * 4));
+      for (int r = threadIdx.x; r < C::kQRows; r += C::kThreads) lse_s[r] = -INFINITY;
+    }
+    __syncwarp();
+    cluster_sync();  // the pieces' rows are in their CTAs' shared memory
+    cluster_merge<MT>(t, smem);
+    __syncwarp();
+    cluster_sync();  // no CTA leaves while another still reads its shared memory
+  }
   if (bars->abort && threadIdx.x == 0) raise_device_error(t.a.err, kErrTimeout);
   if (warp == 2) {
     tc_fence_after();
@@ -866,6 +924,73 @@ __device__ __forceinline__ void store4(const TcArgs& t, int64_t idx, float x, fl
     store_as(t.a.out, t.a.out_dtype, idx + 1, y);
     store_as(t.a.out, t.a.out_dtype, idx + 2, z);
     store_as(t.a.out, t.a.out_dtype, idx + 3, w);
+  }
+}
+
+// The merge of a unit cut between the CTAs of a cluster: CTA c of the
+// cluster finishes packed rows [c * rows / size, (c + 1) * rows / size) of
+// the unit, a warp per row, reading every piece's row and log-sum-exp from
+// the pieces' shared memory (distributed shared memory).  out = sum_j w_j o_j
+// / sum_j w_j with w_j = 2^(lse_j - max lse); pieces that saw no key weigh 0
+// (their rows are never multiplied in), and a row no piece saw is NaN with
+// log-sum-exp -inf, like the single-CTA path.
+constexpr int kMaxCluster = 8;
+
+template <int MT>
+__device__ void cluster_merge(const TcArgs& t, uint8_t* smem) {
+  using C = Cfg<MT>;
+  constexpr int kWarps = C::kThreads / 32;
+  constexpr uint32_t kRowBytes = kD * 4;
+  const AttnArgs& a = t.a;
+  const int nc = t.cluster;
+  const int c = static_cast<int>(blockIdx.x) % nc;
+  const PairInfo pi = pair_info(t, static_cast<int>(blockIdx.x) / nc);
+  const int R = a.group * a.n;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint8_t* part = smem + C::kOffK;
+  const float* lse_s = reinterpret_cast<const float*>(part + C::kQRows * kRowBytes);
+  const int r1 = (c + 1) * C::kQRows / nc;
+#pragma unroll 1
+  for (int row = c * C::kQRows / nc + warp; row < r1; row += kWarps) {
+    const int pr = pi.qg * C::kQRows + row;
+    if (pr >= R) break;  // rows ascend
+    // every load of the row is issued before any result is used
+    const float lj = lane < nc ? ld_cluster_f32(map_shared(lse_s + row, static_cast<uint32_t>(lane))) : -INFINITY;
+    const uint8_t* src = part + row * kRowBytes + ((lane ^ (row & 7)) << 4);
+    float4 v[kMaxCluster];
+#pragma unroll
+    for (int j = 0; j < kMaxCluster; ++j)
+      if (j < nc) v[j] = ld_cluster_v4(map_shared(src, static_cast<uint32_t>(j)));
+    const float M = warp_max(lj);
+    const float wj = (lj == -INFINITY) ? 0.f : ex2_approx(lj - M);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxCluster; ++j) {
+      if (j < nc) {
+        const float w = __shfl_sync(0xffffffffu, wj, j);
+        wsum += w;
+        if (w > 0.f) {
+          acc.x = fmaf(w, v[j].x, acc.x);
+          acc.y = fmaf(w, v[j].y, acc.y);
+          acc.z = fmaf(w, v[j].z, acc.z);
+          acc.w = fmaf(w, v[j].w, acc.w);
+        }
+      }
+    }
+    const int gq = pr / a.n, node = pr - gq * a.n;
+    const int h = pi.kvh * a.group + gq;
+    const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
+    const int64_t ob =
+        static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh + static_cast<int64_t>(node) * a.o_sn;
+    if (M == -INFINITY) {
+      store4(t, ob + lane * 4, NAN, NAN, NAN, NAN);
+      if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
+    } else {
+      const float winv = 1.f / wsum;
+      store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv);
+      if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+    }
   }
 }
 
@@ -1018,7 +1143,22 @@ struct Plan {
   int mt;  // 128-row M-tiles per CTA
   int qgroups, pairs, tiles_per_pair, grid;
   bool varlen, pair_align;
+  int cluster;  // > 1: CTAs per unit in a thread-block cluster (no workspace partials, no merge launch)
 };
+
+template <int MT>
+int cluster_capacity(int size);
+
+// Units cut between the CTAs of a cluster: as many CTAs per unit as the SMs
+// allow (at most 8, the portable cluster size, and no more than the unit has
+// tiles), shrunk until every cluster is resident at once; 0 when fewer than
+// two CTAs per unit fit.
+template <int MT>
+int cluster_size(int pairs, int tiles_per_pair, int sms) {
+  int cl = std::min({kMaxCluster, sms / std::max(1, pairs), tiles_per_pair});
+  while (cl >= 2 && cluster_capacity<MT>(cl) < pairs) --cl;
+  return cl >= 2 ? cl : 0;
+}
 
 template <int MT>
 Plan make_plan_mt(const AttnArgs& a) {
@@ -1049,6 +1189,9 @@ Plan make_plan_mt(const AttnArgs& a) {
       if (cost_pairs * 5 <= ((T + sms - 1) / sms) * 6) {
         pl.pair_align = true;
         pl.grid = static_cast<int>(std::min<int64_t>(sms, pl.pairs));
+      } else if (const int cl = cluster_size<MT>(pl.pairs, pl.tiles_per_pair, sms)) {
+        pl.cluster = cl;
+        pl.grid = pl.pairs * cl;
       } else {
         // at least 4 tiles per CTA so partials stay a small share of the work
         const int64_t g0 = std::max<int64_t>(1, std::min<int64_t>(sms, (T + 3) / 4));
@@ -1101,8 +1244,9 @@ WsLayout ws_layout(const Plan& pl) {
   WsLayout w{};
   size_t off = 0;
   w.tile_start = off; off += align_up(static_cast<size_t>(pl.pairs + 1) * sizeof(int));
-  w.part_lse = off;   off += align_up(static_cast<size_t>(pl.grid) * 2 * rows * sizeof(float));
-  w.part_o = off;     off += align_up(static_cast<size_t>(pl.grid) * 2 * rows * kD * sizeof(float));
+  const size_t slots = pl.cluster ? 0 : static_cast<size_t>(pl.grid) * 2;  // cluster pieces merge in DSMEM
+  w.part_lse = off;   off += align_up(slots * rows * sizeof(float));
+  w.part_o = off;     off += align_up(slots * rows * kD * sizeof(float));
   w.total = off;
   return w;
 }
@@ -1126,6 +1270,45 @@ int ensure_smem_limit(const void* fn, uint32_t bytes) {
   return rc;
 }
 
+// How many clusters of `size` CTAs of the MT kernel can be resident at once
+// (thread-block clusters sit inside one GPC, so this is below SMs / size when
+// the GPCs' SM counts are not multiples of it); once per (device, MT, size).
+template <int MT>
+int cluster_capacity(int size) {
+  static std::mutex mu;
+  static std::vector<std::pair<std::pair<int, int>, int>> cache;  // ((device, size), clusters)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& e : cache)
+      if (e.first.first == dev && e.first.second == size) return e.second;
+  }
+  using C = Cfg<MT>;
+  const void* fn = reinterpret_cast<const void*>(attn_tc_kernel<MT, 2, true>);
+  int n = 0;
+  if (ensure_smem_limit(fn, C::kSmemBytes) == GORGON_OK) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(size));
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(size);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();  // not sticky: clear it, plan without clusters, ask again next time
+      return 0;
+    }
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({{dev, size}, n});
+  return n;
+}
+
 template <int MT>
 int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& kmap, const CUtensorMap& vmap,
               TcArgs& t, cudaStream_t st) {
@@ -1140,6 +1323,21 @@ int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& k
                         : (dtype == GORGON_BF16 ? attn_tc_kernel<MT, 8, true> : attn_tc_kernel<MT, 8, false>);
   rc = ensure_smem_limit(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
+  if (pl.cluster) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(pl.cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, kmap, vmap, t), "tcgen05 tree attention cluster launch");
+  }
   kern<<<pl.grid, C::kThreads, C::kSmemBytes, st>>>(kmap, vmap, t);
   rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
   if (rc || pl.pair_align) return rc;
@@ -1165,7 +1363,7 @@ size_t attn_tc_workspace(const AttnArgs& a) { return ws_layout(make_plan(a)).tot
 void attn_tc_plan(const AttnArgs& a, int32_t* splits, int32_t* launches) {
   const Plan pl = make_plan(a);
   *splits = pl.grid;
-  *launches = 1 + (pl.varlen ? 1 : 0) + (pl.pair_align ? 0 : 1);
+  *launches = 1 + (pl.varlen ? 1 : 0) + (pl.pair_align || pl.cluster ? 0 : 1);
 }
 
 int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st) {
@@ -1212,6 +1410,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.tiles_per_pair = pl.tiles_per_pair;
   t.grid = pl.grid;
   t.pair_align = pl.pair_align;
+  t.cluster = pl.cluster;
   t.ab_fmt = dtype == GORGON_BF16 ? 1 : 0;
   t.wait_ns = wait_limit_ns();
   char* ws = static_cast<char*>(workspace);

@@ -128,6 +128,21 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t p
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr_cluster, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
 }
+// Loads from any CTA of the cluster (a shared::cluster address).  No memory
+// clobber, so that a run of them issues back to back; the cluster barrier
+// that makes the data visible is itself a compiler barrier.
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr_cluster) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr_cluster));
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr_cluster) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr_cluster));
+  return v;
+}
 
 // -------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,

@@ -213,10 +213,12 @@ def _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, sca
         cols = m.shape[2]
         if m.shape[1] != N:
             raise RuntimeError(f"mask has {m.shape[1]} rows for {N} queries")
-        if cols == L:
-            p.mask_kind = _abi.MASK_DENSE
-        elif cols == N:
+        # with no prefix (L == N) the two forms mean the same; the tree form
+        # is the one the tensor-core kernel takes
+        if cols == N:
             p.mask_kind = _abi.MASK_DENSE_TREE
+        elif cols == L:
+            p.mask_kind = _abi.MASK_DENSE
         else:
             raise RuntimeError(f"mask must have {L} (all kv rows) or {N} (tree rows) columns, got {cols}")
         p.mask = m.data_ptr()

@@ -184,3 +184,68 @@ def test_tc_many_pieces_per_unit(grid, out_dtype):
     assert a.dtype == b.dtype
     torch.testing.assert_close(a.float(), b.float(), atol=ATOL, rtol=RTOL)
     torch.testing.assert_close(la, lb, atol=1e-3, rtol=1e-4)
+
+
+# ---- units cut between the CTAs of a thread-block cluster (merged in DSMEM)
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,P", [
+    (1, 32, 8, 64, 2048),    # one sequence: 8 or 16 units, clusters of 8 / 4
+    (2, 32, 8, 64, 8192),    # the one-GPU share of an 8-way sequence split
+    (1, 8, 2, 100, 1500),    # two query groups per kv head, a partly filled unit
+    (1, 4, 4, 256, 900),     # 256-node trees
+    (3, 32, 8, 64, 131),     # few tiles per unit: small clusters, one tile per CTA
+])
+def test_cluster_plan_matches_oracle(B, Hq, Hkv, N, P):
+    pars = _trees(B, N, seed=N + P + 1)
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, seed=P + 1)
+    par_t = torch.tensor(pars, device="cuda")
+    plan = G.tree_attention_plan(q, k, v, parents=par_t, max_depth=5, backend="tcgen05")
+    # one launch, no partials in the workspace (only the unit table remains)
+    assert plan["launches"] == 1 and plan["workspace_bytes"] <= 4096
+    out = G.tree_attention(q, k, v, parents=par_t, max_depth=5, backend="tcgen05")
+    if B * Hq * N * (P + N) <= 40_000_000:
+        ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=np.array(pars), max_depth=5)
+        np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+    else:  # oracle on sampled (sequence, head) slices
+        for b, h in ((0, 0), (B - 1, Hq - 1), (B // 2, Hq // 2 + 1)):
+            ref = O.fused_tree_verify(_np(q[b, h]), _np(k[b, h // (Hq // Hkv)]), _np(v[b, h // (Hq // Hkv)]),
+                                      pars[b], 5)
+            np.testing.assert_allclose(_np(out[b, h]), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_cluster_lse_fp32_and_head_major_output():
+    """The merge writes every output form: fp32 rows, log-sum-exp, and a
+    head-major view (a head-sharded layer's output buffer)."""
+    B, Hq, Hkv, N, P = 2, 32, 8, 64, 1500
+    pars = _trees(B, N, seed=21)
+    q, k, v = _inputs(B, Hq, Hkv, N, P + N, seed=21)
+    par_t = torch.tensor(pars, device="cuda")
+    assert G.tree_attention_plan(q, k, v, parents=par_t, max_depth=5, backend="tcgen05")["launches"] == 1
+    out, lse = G.tree_attention(q, k, v, parents=par_t, max_depth=5, backend="tcgen05",
+                                out_dtype=torch.float32, return_lse=True)
+    _, lse_s = G.tree_attention(q, k, v, parents=par_t, max_depth=5, backend="simt", return_lse=True)
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), parents=np.array(pars), max_depth=5)
+    assert out.dtype == torch.float32
+    np.testing.assert_allclose(_np(out), ref, atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(_np(lse), _np(lse_s), atol=2e-3, rtol=1e-4)
+    full = torch.empty(Hq, B, N, 128, device="cuda", dtype=torch.bfloat16)
+    hm = full.permute(1, 0, 2, 3)
+    G.tree_attention(q, k, v, parents=par_t, max_depth=5, backend="tcgen05", out=hm)
+    np.testing.assert_allclose(_np(hm), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_cluster_row_that_sees_nothing_is_nan():
+    """No prefix and a tree-mask row with no visible node: that row is NaN
+    with log-sum-exp -inf (softmax over nothing), the others match the oracle."""
+    B, Hq, Hkv, N = 1, 8, 8, 200
+    par = _trees(1, N, seed=4, depth=6)[0]
+    m = G.build_tree_mask(par).clone()
+    m[5] = 0
+    q, k, v = _inputs(B, Hq, Hkv, N, N, seed=4)
+    assert G.tree_attention_plan(q, k, v, m, backend="tcgen05")["launches"] == 1
+    out, lse = G.tree_attention(q, k, v, m, backend="tcgen05", return_lse=True)
+    o = _np(out)
+    assert np.isnan(o[:, :, 5]).all() and np.isneginf(_np(lse)[:, :, 5]).all()
+    keep = [i for i in range(N) if i != 5]
+    ref = O.tree_attention_batched(_np(q), _np(k), _np(v), mask=_np(m).astype(bool))
+    np.testing.assert_allclose(o[:, :, keep], ref[:, :, keep], atol=ATOL, rtol=RTOL)

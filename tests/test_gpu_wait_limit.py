@@ -35,21 +35,26 @@ def _case(B, P, seed):
     return q, k, v, pars
 
 
-@pytest.mark.parametrize("backend,B", [("tcgen05-cta", 2), ("tcgen05-pair", 16)])
-def test_wait_that_runs_out_stops_the_kernel_and_reports_it(backend, B):
+@pytest.mark.parametrize("backend,B,splits", [
+    ("tcgen05-cta", 2, None),   # units cut between the CTAs of clusters: every CTA still meets both cluster barriers
+    ("tcgen05-cta", 2, 40),     # stream-K pieces and the merge kernel
+    ("tcgen05-pair", 16, None),
+])
+def test_wait_that_runs_out_stops_the_kernel_and_reports_it(backend, B, splits):
     q, k, v, pars = _case(B, 2000, seed=B)
     par_t = torch.tensor(pars, device="cuda")
+    kw = {} if splits is None else {"num_splits": splits}
     G.device_error(clear=True)
     prev = _abi.set_wait_limit_ns(1)
     try:
-        G.fused_tree_verify(q, k, v, par_t, max_depth=5, backend=backend)
+        G.fused_tree_verify(q, k, v, par_t, max_depth=5, backend=backend, **kw)
         torch.cuda.synchronize()
     finally:
         _abi.set_wait_limit_ns(prev)
     assert prev == 2_000_000_000
     assert G.device_error(clear=True) & _abi.ERR_TIMEOUT
     # the context is intact: the same call with the normal bound is right
-    out = G.fused_tree_verify(q, k, v, par_t, max_depth=5, backend=backend)
+    out = G.fused_tree_verify(q, k, v, par_t, max_depth=5, backend=backend, **kw)
     torch.cuda.synchronize()
     assert G.device_error(clear=True) == 0
     for b, h in ((0, 0), (B - 1, 31)):
