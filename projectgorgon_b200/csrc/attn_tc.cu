@@ -20,9 +20,8 @@
 // at the same time).  With room for two or more CTAs per unit (uniform
 // lengths), each unit is cut into equal tile ranges over the CTAs of one
 // thread-block cluster: every piece leaves its normalised rows and
-// log-sum-exp in its own shared memory, and after a cluster barrier each CTA
-// merges a slice of the unit's rows by reading all pieces through
-// distributed shared memory (one launch, no workspace).  Otherwise (stream-K)
+// log-sum-exp in the workspace, and after a cluster barrier each CTA merges
+// a slice of the unit's rows from L2 (one launch, no merge kernel).  Otherwise (stream-K)
 // the unit-major list of K/V tiles is split into equal contiguous ranges: a
 // unit that falls inside one CTA is finished there; a unit cut between CTAs
 // leaves normalised partials plus log-sum-exp in the workspace, and
@@ -51,6 +50,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 #include <utility>
@@ -90,8 +90,6 @@ struct Cfg {
   // complete, so the shorter ring refills sooner.
   static constexpr bool kSoftmaxFreesK = MT == 2;
   static_assert(kSmemBytes <= 232448, "shared memory per block");
-  // a cluster piece's fp32 rows and log-sum-exp fit in the idle K and V rings
-  static_assert(kQRows * (kD * 4 + 4) <= 2 * kStages * kTileBytes, "cluster partials");
   static_assert(2 * MT * kBN <= kColO, "S buffers below O");
 };
 
@@ -104,6 +102,7 @@ struct TcArgs {
   int grid;
   int pair_align;     // whole units per CTA, strided by the grid (no partials to merge)
   int cluster;        // > 1: each unit cut between the CTAs of a cluster of this size, merged in DSMEM
+  int q_tma;          // Q M-tiles come by TMA (tree size divides 128 or is a multiple of it)
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // 16-byte aligned output rows: kOutBf16 / kOutF16 / kOutF32, else 0
   float* part_o;      // [grid * 2][rows per unit][128]
@@ -119,6 +118,7 @@ struct Barriers {
   uint64_t v_full[Cfg<MT>::kStages];
   uint64_t v_empty[Cfg<MT>::kStages];
   uint64_t q_full;
+  uint64_t q_empty;         // (Q by TMA) the softmax warps are done with the Q tile as output staging
   // per (S buffer, M-tile): index buf * MT + mtile
   uint64_t s_full[2 * MT];
   uint64_t p_full[2 * MT];
@@ -209,9 +209,29 @@ struct Segments {
 // ------------------------------------------------------------ roles
 // Streams one operand (K when is_v == 0, else V) of every tile of the CTA's
 // segments through its ring.
+// The Q rows of one unit (MT M-tiles, two 64-column SW128 boxes each) by
+// TMA: a box of 128 / n heads x n nodes (or 128 of the nodes) is 128
+// consecutive packed rows.  Rows past the unit's real rows read the next
+// heads' rows (or zeros past the last head); nothing reads their results.
 template <int MT>
-__device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem, Barriers<MT>* bars, int64_t g0,
-                         int64_t g1, int is_v) {
+__device__ __forceinline__ void load_q_tma(const TcArgs& t, const CUtensorMap* qmap, uint8_t* smem,
+                                           Barriers<MT>* bars, const PairInfo& pi) {
+  const AttnArgs& a = t.a;
+  mbar_arrive_expect_tx(&bars->q_full, MT * 2 * kQHalf);
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    const int pr0 = pi.qg * Cfg<MT>::kQRows + mt * kBM;
+    const int gq = pr0 / a.n, node = pr0 - gq * a.n;
+    const int head = pi.kvh * a.group + gq;
+    uint8_t* dst = smem + kOffQ + mt * 2 * kQHalf;
+    tma_load_4d_hint(dst, qmap, &bars->q_full, 0, node, head, pi.b, l2_policy_evict_first());
+    tma_load_4d_hint(dst + kQHalf, qmap, &bars->q_full, 64, node, head, pi.b, l2_policy_evict_first());
+  }
+}
+
+template <int MT>
+__device__ void producer(const TcArgs& t, const CUtensorMap* map, const CUtensorMap* qmap, uint8_t* smem,
+                         Barriers<MT>* bars, int64_t g0, int64_t g1, int is_v) {
   using C = Cfg<MT>;
   volatile int* abort = &bars->abort;
   uint64_t* full = is_v ? bars->v_full : bars->k_full;
@@ -226,7 +246,14 @@ __device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem,
   int64_t g, e;
   PairInfo pi;
   bool ok = true;
+  uint32_t q_loads = 0;  // Q tiles issued by TMA (K producer only)
   while (ok && sg.next(t, g, e, pi)) {
+    if (t.q_tma && !is_v) {
+      // the previous unit's epilogue has finished with the Q tile
+      if (q_loads > 0 && !bounded_wait(&bars->q_empty, (q_loads - 1) & 1u, abort, t.wait_ns)) break;
+      load_q_tma<MT>(t, qmap, smem, bars, pi);
+      ++q_loads;
+    }
     for (; g < e; ++g) {
       const int tile = static_cast<int>(g - pi.start);
       const int stage = static_cast<int>(issued % C::kStages);
@@ -252,6 +279,7 @@ __device__ void producer(const TcArgs& t, const CUtensorMap* map, uint8_t* smem,
   // Every issued load must land before the CTA leaves.
   for (int64_t k = (issued > C::kStages ? issued - C::kStages : 0); k < issued; ++k)
     drain_wait(&full[k % C::kStages], static_cast<uint32_t>(k / C::kStages) & 1u);
+  if (q_loads > 0) drain_wait(&bars->q_full, (q_loads - 1) & 1u);
 }
 
 // Ring position of a tile counter, advanced without divisions.
@@ -403,7 +431,7 @@ __device__ void pv_issuer(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, ui
 }
 
 
-template <int MT, int ANCW, bool BF16>
+template <int MT, int ANCW, bool BF16, bool QTMA>
 __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* bars, uint32_t tmem, int64_t g0,
                                  int64_t g1, int cta) {
   using C = Cfg<MT>;
@@ -421,6 +449,15 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
   constexpr bool ab_bf16 = BF16;  // P's 16-bit type (that of Q, K and V)
   const int qrow = wg * kBM + r;                // row within the unit
   int64_t i = 0;
+  // (Q by TMA) the warp hands the Q tile back to the producer once its
+  // output staging in it is done: generic-proxy accesses before the TMA writes
+  auto q_done = [&]() {
+    if (QTMA) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->q_empty);
+    }
+  };
   Segments sg(g0, g1);
   int64_t g, e;
   PairInfo pi;
@@ -441,7 +478,7 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     // cache lines per instruction and keep the load unit busy for
     // microseconds); 8 rows per half-warp are in flight per round trip.
     const bool walk = a.mask_kind == GORGON_MASK_PARENTS;
-    {
+    if (!QTMA) {
       const int sub = lane >> 4, jc = lane & 15;  // row parity and 16-byte chunk
       const int prow0 = pi.qg * C::kQRows + wg * kBM + wq * 32 + sub;  // packed row of the first pass
       const __nv_bfloat16* qb = static_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(pi.b) * a.q_sb +
@@ -659,31 +696,6 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     const int mode = whole ? t.out_vec : kOutF32;
     const float inv = 1.f / l;  // whole, l == 0: no visible key, NaN like softmax
     const bool zero = !whole && !(l > 0.f);
-    if (t.cluster) {
-      // A piece of a unit cut between the CTAs of a cluster: the normalised
-      // row (0 where nothing was visible) and its log-sum-exp stay in this
-      // CTA's shared memory (the K and V rings, idle once the last P.V has
-      // completed), where cluster_merge reads them.  16-byte chunk j of row q
-      // sits at chunk j ^ (q & 7), so both a warp's row-per-thread stores and
-      // the merge's row-per-warp loads use every bank.
-      uint8_t* prow = smem + C::kOffK + static_cast<uint32_t>(qrow) * (kD * 4);
-#pragma unroll
-      for (int ch = 0; ch < kD / 32; ++ch) {
-        uint32_t ov[32];
-        tmem_ld32(o_addr + ch * 32, ov);
-        tmem_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int j = ch * 8 + u;
-          *reinterpret_cast<float4*>(prow + ((j ^ (qrow & 7)) << 4)) =
-              zero ? make_float4(0.f, 0.f, 0.f, 0.f)
-                   : make_float4(__uint_as_float(ov[4 * u]) * inv, __uint_as_float(ov[4 * u + 1]) * inv,
-                                 __uint_as_float(ov[4 * u + 2]) * inv, __uint_as_float(ov[4 * u + 3]) * inv);
-        }
-      }
-      reinterpret_cast<float*>(smem + C::kOffK + C::kQRows * (kD * 4))[qrow] = lse2;
-      continue;
-    }
     if (mode == kOutBf16 || mode == kOutF16) {
 #pragma unroll
       for (int ch = 0; ch < kD / 32; ++ch) {
@@ -768,16 +780,20 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
     } else {
       t.part_lse[slot * C::kQRows + qrow] = lse2;  // attn_tc_combine merges the pieces
     }
+    q_done();
   }
 }
 
 template <int MT>
-__device__ void cluster_merge(const TcArgs& t, uint8_t* smem);
+__device__ void cluster_merge(const TcArgs& t);
 
-template <int MT, int ANCW, bool BF16>
+// QTMA: the Q M-tiles come by TMA from the K producer (t.q_tma), so the
+// softmax warps skip their own Q loads (a compile-time switch: as a run-time
+// branch it cost the hot loop registers).
+template <int MT, int ANCW, bool BF16, bool QTMA>
 __global__ void __launch_bounds__(Cfg<MT>::kThreads, 1)
 attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-               const __grid_constant__ TcArgs t) {
+               const __grid_constant__ CUtensorMap qmap, const __grid_constant__ TcArgs t) {
   using C = Cfg<MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -792,7 +808,8 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
       mbar_init(&bars->v_full[s], 1);
       mbar_init(&bars->v_empty[s], 1);
     }
-    mbar_init(&bars->q_full, 4 * MT);  // every softmax warp
+    mbar_init(&bars->q_full, t.q_tma ? 1 : 4 * MT);  // the K producer's expect-tx, else every softmax warp
+    mbar_init(&bars->q_empty, 4 * MT);
     for (int b = 0; b < 2 * MT; ++b) {
       mbar_init(&bars->s_full[b], 1);
       mbar_init(&bars->p_full[b], 4);  // the four warps of one softmax warpgroup
@@ -807,6 +824,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&kmap);
     prefetch_tensormap(&vmap);
+    if (t.q_tma) prefetch_tensormap(&qmap);
   }
   if (warp == 2) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
@@ -838,32 +856,27 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 
   if (work) {
     if (warp == 0) {
-      if (lane == 0) producer<MT>(t, &kmap, smem, bars, g0, g1, 0);
+      if (lane == 0) producer<MT>(t, &kmap, &qmap, smem, bars, g0, g1, 0);
     } else if (warp == 3) {
-      if (lane == 0) producer<MT>(t, &vmap, smem, bars, g0, g1, 1);
+      if (lane == 0) producer<MT>(t, &vmap, &qmap, smem, bars, g0, g1, 1);
     } else if (warp == 1) {
       if (lane == 0) qk_issuer<MT>(t, smem, bars, tmem, g0, g1);
     } else if (warp == 2) {
       if (lane == 0) pv_issuer<MT>(t, smem, bars, tmem, g0, g1);
     } else if (warp >= 4) {
-      softmax_epilogue<MT, ANCW, BF16>(t, smem, bars, tmem, g0, g1, blockIdx.x);
+      softmax_epilogue<MT, ANCW, BF16, QTMA>(t, smem, bars, tmem, g0, g1, blockIdx.x);
     }
   }
   __syncwarp();  // role warps ran their loop on lane 0: reconverge before the CTA barrier
   tc_fence_before();
   __syncthreads();
   if (t.cluster) {
-    // Every thread of every CTA of the cluster passes both barriers (the roles
+    // Every thread of every CTA of the cluster passes the barrier (the roles
     // return here on every path, a timeout included).
-    if (!work) {  // a piece with no tiles contributes nothing
-      float* lse_s = reinterpret_cast<float*>(smem + C::kOffK + C::kQRows * (kD * 4));
-      for (int r = threadIdx.x; r < C::kQRows; r += C::kThreads) lse_s[r] = -INFINITY;
-    }
+    __threadfence();  // the piece's rows (written by its softmax warps) before the barrier's release
     __syncwarp();
-    cluster_sync();  // the pieces' rows are in their CTAs' shared memory
-    cluster_merge<MT>(t, smem);
-    __syncwarp();
-    cluster_sync();  // no CTA leaves while another still reads its shared memory
+    cluster_sync();   // every piece of the cluster's unit is in the workspace
+    cluster_merge<MT>(t);
   }
   if (bars->abort && threadIdx.x == 0) raise_device_error(t.a.err, kErrTimeout);
   if (warp == 2) {
@@ -927,70 +940,112 @@ __device__ __forceinline__ void store4(const TcArgs& t, int64_t idx, float x, fl
   }
 }
 
-// The merge of a unit cut between the CTAs of a cluster: CTA c of the
-// cluster finishes packed rows [c * rows / size, (c + 1) * rows / size) of
-// the unit, a warp per row, reading every piece's row and log-sum-exp from
-// the pieces' shared memory (distributed shared memory).  out = sum_j w_j o_j
-// / sum_j w_j with w_j = 2^(lse_j - max lse); pieces that saw no key weigh 0
+// The merge of a unit cut between the CTAs of a cluster: every piece leaves
+// its normalised fp32 rows and log-sum-exp in its workspace slot (like a
+// stream-K piece), and after the cluster barrier CTA c of the cluster
+// finishes packed rows [c * rows / size, (c + 1) * rows / size) of the unit,
+// a warp per row, reading the pieces' rows from L2.  out = sum_j w_j o_j /
+// sum_j w_j with w_j = 2^(lse_j - max lse); pieces that saw no key weigh 0
 // (their rows are never multiplied in), and a row no piece saw is NaN with
-// log-sum-exp -inf, like the single-CTA path.
+// log-sum-exp -inf, like the single-CTA path.  A warp issues the loads of
+// 16 / size of its rows before it uses any, one round trip per batch.
+// Measured against reading the pieces from the other CTAs' shared memory
+// (distributed shared memory): ~64 KB per CTA took 3.3-3.5 us that way.
 constexpr int kMaxCluster = 8;
+constexpr int kMergeSlots = 16;  // (row, piece) loads in flight per lane
 
-template <int MT>
-__device__ void cluster_merge(const TcArgs& t, uint8_t* smem) {
+template <int MT, int NC>
+__device__ void cluster_merge_n(const TcArgs& t) {
   using C = Cfg<MT>;
   constexpr int kWarps = C::kThreads / 32;
-  constexpr uint32_t kRowBytes = kD * 4;
+  constexpr int kRows = kMergeSlots / NC;  // rows per batch
   const AttnArgs& a = t.a;
-  const int nc = t.cluster;
-  const int c = static_cast<int>(blockIdx.x) % nc;
-  const PairInfo pi = pair_info(t, static_cast<int>(blockIdx.x) / nc);
+  const int c = static_cast<int>(blockIdx.x) % NC;
+  const int unit = static_cast<int>(blockIdx.x) / NC;
+  const PairInfo pi = pair_info(t, unit);
   const int R = a.group * a.n;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint8_t* part = smem + C::kOffK;
-  const float* lse_s = reinterpret_cast<const float*>(part + C::kQRows * kRowBytes);
-  const int r1 = (c + 1) * C::kQRows / nc;
+  // piece j of the unit is CTA unit * NC + j, workspace slot 2 * (unit * NC + j)
+  const int64_t slot0 = static_cast<int64_t>(unit) * NC * 2;
+  // this CTA's rows that are real packed rows: [r0, r1)
+  const int r0 = c * C::kQRows / NC;
+  const int r1 = min((c + 1) * C::kQRows / NC, R - pi.qg * C::kQRows);
 #pragma unroll 1
-  for (int row = c * C::kQRows / nc + warp; row < r1; row += kWarps) {
-    const int pr = pi.qg * C::kQRows + row;
-    if (pr >= R) break;  // rows ascend
-    // every load of the row is issued before any result is used
-    const float lj = lane < nc ? ld_cluster_f32(map_shared(lse_s + row, static_cast<uint32_t>(lane))) : -INFINITY;
-    const uint8_t* src = part + row * kRowBytes + ((lane ^ (row & 7)) << 4);
-    float4 v[kMaxCluster];
+  for (int rb = r0 + warp; rb < r1; rb += kWarps * kRows) {
+    // lane k * NC + j holds piece j's log-sum-exp of batch row k (-inf for a
+    // piece with no tiles, which wrote nothing: the planner gives every CTA
+    // at least one tile, but the merge does not rely on it)
+    float lj = -INFINITY;
+    {
+      const int k = lane / NC, j = lane - (lane / NC) * NC;
+      const int row = rb + kWarps * k;
+      const int64_t nt = pi.end - pi.start;
+      if (k < kRows && row < r1 && nt * (j + 1) / NC > nt * j / NC)
+        lj = __ldcg(t.part_lse + (slot0 + 2 * j) * C::kQRows + row);
+    }
+    float4 v[kRows][NC];
 #pragma unroll
-    for (int j = 0; j < kMaxCluster; ++j)
-      if (j < nc) v[j] = ld_cluster_v4(map_shared(src, static_cast<uint32_t>(j)));
-    const float M = warp_max(lj);
-    const float wj = (lj == -INFINITY) ? 0.f : ex2_approx(lj - M);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
+    for (int k = 0; k < kRows; ++k) {
+      const int row = rb + kWarps * k;
+      if (row < r1) {
 #pragma unroll
-    for (int j = 0; j < kMaxCluster; ++j) {
-      if (j < nc) {
-        const float w = __shfl_sync(0xffffffffu, wj, j);
-        wsum += w;
-        if (w > 0.f) {
-          acc.x = fmaf(w, v[j].x, acc.x);
-          acc.y = fmaf(w, v[j].y, acc.y);
-          acc.z = fmaf(w, v[j].z, acc.z);
-          acc.w = fmaf(w, v[j].w, acc.w);
-        }
+        for (int j = 0; j < NC; ++j)
+          v[k][j] = __ldcg(reinterpret_cast<const float4*>(t.part_o + ((slot0 + 2 * j) * C::kQRows + row) * kD) + lane);
       }
     }
-    const int gq = pr / a.n, node = pr - gq * a.n;
-    const int h = pi.kvh * a.group + gq;
-    const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
-    const int64_t ob =
-        static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh + static_cast<int64_t>(node) * a.o_sn;
-    if (M == -INFINITY) {
-      store4(t, ob + lane * 4, NAN, NAN, NAN, NAN);
-      if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
-    } else {
-      const float winv = 1.f / wsum;
-      store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv);
-      if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+#pragma unroll
+    for (int k = 0; k < kRows; ++k) {
+      const int row = rb + kWarps * k;
+      float lk[NC];
+      float M = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        lk[j] = __shfl_sync(0xffffffffu, lj, k * NC + j);
+        M = fmaxf(M, lk[j]);
+      }
+      if (row >= r1) continue;  // warp-uniform
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float wsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        const float w = (lk[j] == -INFINITY) ? 0.f : ex2_approx(lk[j] - M);
+        wsum += w;
+        if (w > 0.f) {
+          acc.x = fmaf(w, v[k][j].x, acc.x);
+          acc.y = fmaf(w, v[k][j].y, acc.y);
+          acc.z = fmaf(w, v[k][j].z, acc.z);
+          acc.w = fmaf(w, v[k][j].w, acc.w);
+        }
+      }
+      const int pr = pi.qg * C::kQRows + row;
+      const int gq = pr / a.n, node = pr - gq * a.n;
+      const int h = pi.kvh * a.group + gq;
+      const int64_t orow = (static_cast<int64_t>(pi.b) * a.hq + h) * a.n + node;
+      const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
+                         static_cast<int64_t>(node) * a.o_sn;
+      if (M == -INFINITY) {
+        store4(t, ob + lane * 4, NAN, NAN, NAN, NAN);
+        if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
+      } else {
+        const float winv = 1.f / wsum;
+        store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv);
+        if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
+      }
     }
+  }
+}
+
+template <int MT>
+__device__ void cluster_merge(const TcArgs& t) {
+  switch (t.cluster) {
+    case 2: cluster_merge_n<MT, 2>(t); break;
+    case 3: cluster_merge_n<MT, 3>(t); break;
+    case 4: cluster_merge_n<MT, 4>(t); break;
+    case 5: cluster_merge_n<MT, 5>(t); break;
+    case 6: cluster_merge_n<MT, 6>(t); break;
+    case 7: cluster_merge_n<MT, 7>(t); break;
+    case 8: cluster_merge_n<MT, 8>(t); break;
+    default: break;
   }
 }
 
@@ -1244,7 +1299,7 @@ WsLayout ws_layout(const Plan& pl) {
   WsLayout w{};
   size_t off = 0;
   w.tile_start = off; off += align_up(static_cast<size_t>(pl.pairs + 1) * sizeof(int));
-  const size_t slots = pl.cluster ? 0 : static_cast<size_t>(pl.grid) * 2;  // cluster pieces merge in DSMEM
+  const size_t slots = static_cast<size_t>(pl.grid) * 2;
   w.part_lse = off;   off += align_up(slots * rows * sizeof(float));
   w.part_o = off;     off += align_up(slots * rows * kD * sizeof(float));
   w.total = off;
@@ -1285,7 +1340,7 @@ int cluster_capacity(int size) {
       if (e.first.first == dev && e.first.second == size) return e.second;
   }
   using C = Cfg<MT>;
-  const void* fn = reinterpret_cast<const void*>(attn_tc_kernel<MT, 2, true>);
+  const void* fn = reinterpret_cast<const void*>(attn_tc_kernel<MT, 2, true, true>);
   int n = 0;
   if (ensure_smem_limit(fn, C::kSmemBytes) == GORGON_OK) {
     cudaLaunchConfig_t cfg = {};
@@ -1311,7 +1366,7 @@ int cluster_capacity(int size) {
 
 template <int MT>
 int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& kmap, const CUtensorMap& vmap,
-              TcArgs& t, cudaStream_t st) {
+              const CUtensorMap& qmap, TcArgs& t, cudaStream_t st) {
   using C = Cfg<MT>;
   int rc = GORGON_OK;
   if (pl.varlen) {
@@ -1319,8 +1374,15 @@ int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& k
     rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
     if (rc) return rc;
   }
-  auto kern = a.n <= 64 ? (dtype == GORGON_BF16 ? attn_tc_kernel<MT, 2, true> : attn_tc_kernel<MT, 2, false>)
-                        : (dtype == GORGON_BF16 ? attn_tc_kernel<MT, 8, true> : attn_tc_kernel<MT, 8, false>);
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const TcArgs);
+  Kern kern;
+  const bool bf = dtype == GORGON_BF16;
+  if (t.q_tma)
+    kern = a.n <= 64 ? (bf ? attn_tc_kernel<MT, 2, true, true> : attn_tc_kernel<MT, 2, false, true>)
+                     : (bf ? attn_tc_kernel<MT, 8, true, true> : attn_tc_kernel<MT, 8, false, true>);
+  else
+    kern = a.n <= 64 ? (bf ? attn_tc_kernel<MT, 2, true, false> : attn_tc_kernel<MT, 2, false, false>)
+                     : (bf ? attn_tc_kernel<MT, 8, true, false> : attn_tc_kernel<MT, 8, false, false>);
   rc = ensure_smem_limit(reinterpret_cast<const void*>(kern), C::kSmemBytes);
   if (rc) return rc;
   if (pl.cluster) {
@@ -1336,9 +1398,9 @@ int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& k
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return check_cuda(cudaLaunchKernelEx(&cfg, kern, kmap, vmap, t), "tcgen05 tree attention cluster launch");
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, kmap, vmap, qmap, t), "tcgen05 tree attention cluster launch");
   }
-  kern<<<pl.grid, C::kThreads, C::kSmemBytes, st>>>(kmap, vmap, t);
+  kern<<<pl.grid, C::kThreads, C::kSmemBytes, st>>>(kmap, vmap, qmap, t);
   rc = check_cuda(cudaGetLastError(), "tcgen05 tree attention launch");
   if (rc || pl.pair_align) return rc;
   attn_tc_combine<MT><<<dim3(pl.pairs, C::kQRows / kCombineRows), kCombineThreads, 0, st>>>(t);
@@ -1425,7 +1487,28 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
                         : a.out_dtype == GORGON_BF16 ? kOutBf16
                                                      : (a.out_dtype == GORGON_F16 ? kOutF16 : kOutF32);
   }
-  return pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, t, st) : launch_mt<2>(a, dtype, pl, kmap, vmap, t, st);
+  // Q by TMA when a 128-row M-tile is whole heads (n divides 128) or part of
+  // one (n a multiple of 128): a 4-D box (64 columns, nodes, heads, 1) over
+  // q [B, Hq, n, D] is then 128 consecutive packed rows.  Cluster plans only:
+  // their CTAs have few tiles, so the earlier first Q.K^T shows (one
+  // sequence over 2048 tokens 16.3 -> 15.4 us, two over 8192 32.7 -> 31.6);
+  // whole-unit plans measured ~1 % slower with it.
+  CUtensorMap qmap;
+  std::memset(&qmap, 0, sizeof(qmap));
+  if (pl.cluster && (kBM % a.n == 0 || a.n % kBM == 0) && a.q_sn > 0) {
+    const int nb = a.n < kBM ? a.n : kBM;
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(a.n),
+                                static_cast<cuuint64_t>(a.hq), static_cast<cuuint64_t>(a.batch)};
+    const cuuint64_t strides[3] = {static_cast<cuuint64_t>(a.q_sn) * 2, static_cast<cuuint64_t>(a.q_sh) * 2,
+                                   static_cast<cuuint64_t>(a.q_sb) * 2};
+    const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(nb), static_cast<cuuint32_t>(kBM / nb), 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    t.q_tma = enc(&qmap, tdt, 4, const_cast<void*>(a.q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  return pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, qmap, t, st)
+                    : launch_mt<2>(a, dtype, pl, kmap, vmap, qmap, t, st);
 }
 
 }  // namespace gorgon
