@@ -19,8 +19,9 @@ with the time each stage takes on its own stream.
 Multi-GPU (torchrun, one rank per GPU): by default the workload's batch is
 split by sequence over the ranks (strong scaling: the same layer on more
 GPUs, no collective on the data path); ``--shard weak`` gives every rank a
-batch of its own, ``--shard heads`` splits one layer by kv head with an NCCL
-all-gather of the output.  The timing is the max over ranks.
+batch of its own, ``--shard heads`` splits one layer by kv head, the output
+gathered by the attention kernel itself over NVLink (``--gather nccl``: an
+NCCL all-gather after it).  The timing is the max over ranks.
 """
 from __future__ import annotations
 
@@ -173,7 +174,7 @@ def seq_shard(name: str, world: int, rank: int, mode: str):
     return s, e - s
 
 
-def attn_config(name: str, world: int, mode: str) -> dict:
+def attn_config(name: str, world: int, mode: str, gather: str = "fused") -> dict:
     """The `config` of an attention workload's JSON line: the same dict for
     this build's arm and the reference arm (it needs no GPU)."""
     cfg = WORKLOADS[name]
@@ -191,8 +192,9 @@ def attn_config(name: str, world: int, mode: str) -> dict:
     elif mode == "weak":
         par = f"sequence-sharded x{world}, weak scaling: {B} sequences per GPU, {B * world} in all"
     elif mode == "heads":
-        par = (f"kv-head-sharded x{world}, strong scaling: {cfg['Hkv'] // world} of {cfg['Hkv']} kv heads per GPU, "
-               f"one NCCL all-gather of the output")
+        how = ("the output gather fused into the attention (NVLink stores to every GPU's buffer)"
+               if gather == "fused" else "one NCCL all-gather of the output")
+        par = f"kv-head-sharded x{world}, strong scaling: {cfg['Hkv'] // world} of {cfg['Hkv']} kv heads per GPU, {how}"
     else:
         par = (f"sequence-sharded x{world}, strong scaling: the batch of {B} sequences split "
                f"{'/'.join(str(n) for n in per_gpu)} over the GPUs, no collective on the data path")
@@ -286,7 +288,7 @@ class Workload:
     graphable = True  # one step is one stream-ordered public call
 
     def config(self, world: int, plan: dict) -> dict:
-        return attn_config(self.name, world, self.mode)
+        return attn_config(self.name, world, self.mode, getattr(self, "gather", "fused"))
 
     def extra(self, world: int, ms_step: float) -> dict:
         return {"us_per_layer": round(ms_step * 1e3, 2),
@@ -319,13 +321,16 @@ class HeadShardWorkload(Workload):
 
     scaling = "strong"
 
-    def __init__(self, name: str, dev: torch.device, rank: int, world: int, chunks: int = 1):
+    def __init__(self, name: str, dev: torch.device, rank: int, world: int, chunks: int = 1,
+                 gather: str = "fused"):
         cfg = WORKLOADS[name]
         if isinstance(cfg["P"], tuple):
             raise SystemExit("--shard heads needs a workload with one prefix length")
         if cfg["B"] % chunks:
             raise SystemExit(f"--head-chunks {chunks} does not divide the batch of {cfg['B']}")
-        self.chunks = chunks
+        if gather == "fused" and chunks != 1:
+            raise SystemExit("--head-chunks applies to --gather nccl")
+        self.chunks, self.gather = chunks, gather
         self.name, self.cfg, self.dev = name, cfg, dev
         B, Hq, Hkv, D, N, P = cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["D"], cfg["N"], cfg["P"]
         (h0, h1), (q0, q1) = sharding.shard_heads(Hkv, Hq, world, rank)
@@ -355,11 +360,21 @@ class HeadShardWorkload(Workload):
         # one contiguous piece of each chunk's buffer, which the attention
         # writes and the in-place all-gather sends; chunk c's gather runs on
         # NCCL's stream while chunk c + 1's attention computes
-        Bc = B // chunks
-        bufs = [sharding.head_sharded_output(Bc, Hq, N, D, dt, dev, world, rank) for _ in range(chunks)]
-        self.fulls = [f for f, _ in bufs]
-        self.locals = [l for _, l in bufs]
-        self.full, self.local = bufs[0]
+        self.peers = []
+        if gather == "fused":
+            # the gather fused into the attention: every rank's heads go
+            # straight into every rank's buffer over NVLink (two buffers, so
+            # that an end-to-end step's copy-out overlaps the next step)
+            self.peers = [sharding.PeerHeadOutput(B, Hq, Hkv, N, D, dt, dev, world, rank) for _ in range(2)]
+            self.full, self.local = self.peers[0].full_head_major, self.peers[0].local
+            self.fulls, self.locals = [self.full], [self.local]
+            self.graphable = True  # no collective call in the step
+        else:
+            Bc = B // chunks
+            bufs = [sharding.head_sharded_output(Bc, Hq, N, D, dt, dev, world, rank) for _ in range(chunks)]
+            self.fulls = [f for f, _ in bufs]
+            self.locals = [l for _, l in bufs]
+            self.full, self.local = bufs[0]
         self.out = torch.empty(B, Hq, N, D, device=dev, dtype=dt)  # shape only (the e2e copy-out buffer)
         esz = torch.tensor([], dtype=dt).element_size()
         # this rank's share: its K/V, Q and output slice, and the parents
@@ -371,6 +386,9 @@ class HeadShardWorkload(Workload):
     def step(self):
         st = torch.cuda.current_stream(self.dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if self.gather == "fused":
+            peer = self.peers[0]
+            return G.fused_tree_verify(self.q, self.k, self.v, out=peer.local, peer_group=peer, **self.kwargs())
         if self.chunks == 1:
             e0.record(st)
             G.fused_tree_verify(self.q, self.k, self.v, out=self.local, **self.kwargs())
@@ -398,14 +416,36 @@ class HeadShardWorkload(Workload):
         """The output gather of one e2e step (a fresh buffer per step)."""
         return sharding.gather_heads(o)
 
+    @property
+    def persistent_out(self) -> bool:
+        """End-to-end steps write the peer buffers (``e2e_step``), not a fresh tensor."""
+        return self.gather == "fused"
+
+    def e2e_step(self, k: int, q_d: torch.Tensor, par_d: torch.Tensor):
+        """(fused gather) One end-to-end step's attention into buffer set k:
+        the returned ``[B, Hq, N, D]`` view is the layer on this rank."""
+        peer = self.peers[k]
+        G.fused_tree_verify(q_d, self.k, self.v, out=peer.local, peer_group=peer,
+                            **dict(self.kwargs(), parents=par_d))
+        return peer.full
+
+    def close(self):
+        for p in self.peers:
+            p.close()
+        self.peers = []
+
     mode = "heads"
-    graphable = False  # the step holds an NCCL all-gather: timed eagerly
+    graphable = False  # with --gather nccl the step holds an all-gather: timed eagerly
 
     def extra(self, world: int, ms_step: float) -> dict:
+        if self.gather == "fused":
+            return {"us_per_layer": round(ms_step * 1e3, 2), "gather": "fused into the attention epilogue "
+                    "(NVLink stores to every rank's buffer, on-device completion counters)",
+                    "tokens_verified_per_s": round(self.tokens / (ms_step * 1e-3), 1)}
         ev = self.kernel_events
         torch.cuda.synchronize(self.dev)
         k_ms = float(np.mean([a.elapsed_time(b) for a, b in ev])) if ev else float("nan")
-        return {"us_per_layer": round(ms_step * 1e3, 2), "kernel_only_us": round(k_ms * 1e3, 2),
+        return {"us_per_layer": round(ms_step * 1e3, 2), "gather": "NCCL all-gather", "kernel_only_us": round(k_ms * 1e3, 2),
                 "allgather_us": round((ms_step - k_ms) * 1e3, 2),
                 "tokens_verified_per_s": round(self.tokens / (ms_step * 1e-3), 1)}
 
@@ -1110,6 +1150,7 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     in_ready2 = [torch.cuda.Event() for _ in range(nbuf)]
     in_free = [torch.cuda.Event() for _ in range(nbuf)]
     done = [torch.cuda.Event() for _ in range(nbuf)]
+    out_free = [torch.cuda.Event() for _ in range(nbuf)]
     kw = wl.kwargs()
     # per-step stamps of each stage, on the stream that runs it: copy-in (both
     # copy streams), compute (the tree rows' cache write and the attention),
@@ -1153,9 +1194,17 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
         else:
             wl.k[:, :, P:P + N].copy_(kt_d)
             wl.v[:, :, P:P + N].copy_(vt_d)
-        o = G.fused_tree_verify(q_d, wl.k, wl.v, **dict(kw, parents=par_d))
-        if post is not None:
-            o = post(o)
+        e2e_step = wl.e2e_step if getattr(wl, "persistent_out", False) else None
+        if e2e_step is not None:
+            # output in a persistent buffer (one per buffer set): written
+            # again two steps later, once this step's copy-out has read it
+            if i >= nbuf:
+                s_c.wait_event(out_free[k])
+            o = e2e_step(k, q_d, par_d)
+        else:
+            o = G.fused_tree_verify(q_d, wl.k, wl.v, **dict(kw, parents=par_d))
+            if post is not None:
+                o = post(o)
         if rec:
             st[5].record(s_c)
         in_free[k].record(s_c)
@@ -1167,7 +1216,9 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
             outs_h[k].copy_(o, non_blocking=True)
             if rec:
                 st[7].record(s_out)
-            o.record_stream(s_out)
+            out_free[k].record(s_out)
+            if e2e_step is None:
+                o.record_stream(s_out)
         if rec:
             stamps.append(st)
 
@@ -1250,7 +1301,7 @@ def run_ours(args):
     if args.shard == "heads":
         if kind != "attn":
             raise SystemExit("--shard heads applies to the attention workloads")
-        wl = HeadShardWorkload(args.workload, dev, rank, world, chunks=args.head_chunks)
+        wl = HeadShardWorkload(args.workload, dev, rank, world, chunks=args.head_chunks, gather=args.gather)
     elif kind == "attn":
         # strong (default): the fixed batch split over the ranks; weak: a batch per rank
         mode = "weak" if args.shard == "weak" else "strong"
@@ -1274,6 +1325,8 @@ def run_ours(args):
     e2e_parts = e2e[4] if len(e2e) > 4 else None
     e2e_ms = max_over_ranks(e2e_ms, world, dev)
     extra = wl.extra(world, total_ms / args.steps)
+    if hasattr(wl, "close"):
+        wl.close()  # peer buffers: every rank unmaps and frees them together
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -1463,7 +1516,7 @@ def run_reference(args):
         "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
         "scaling": "weak" if mode == "weak" else "strong", "vs_baseline": None, "dtype": cfg["dtype"],
         "data": Workload.data,
-        "config": attn_config(args.workload, world, mode),
+        "config": attn_config(args.workload, world, mode, args.gather),
         "sequences_per_step": per_step,
         "us_per_layer": round(step_s * 1e6 * cfg["B"] / per_step, 1),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": ha.cores, "kind": ha.kind,
@@ -1578,8 +1631,10 @@ def main():
     ap.add_argument("--shard", default="sequences", choices=["sequences", "weak", "heads"],
                     help="multi-GPU split: the workload's batch divided by sequence over the ranks (strong "
                          "scaling, default), a whole batch per rank (weak scaling), or one layer's kv heads "
-                         "per rank with an NCCL all-gather of the output (strong scaling)")
+                         "per rank with the output gathered over NVLink (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="--shard heads: output gather fused into the attention (NVLink stores) or an NCCL all-gather")
     ap.add_argument("--head-chunks", type=int, default=1,
                     help="--shard heads: batch chunks whose all-gathers overlap the next chunk's attention")
     ap.add_argument("--eager", action="store_true",

@@ -159,6 +159,57 @@ GORGON_API int gorgon_tree_attn_plan(const gorgon_tree_attn_params* p, int32_t* 
                           int32_t* splits, int32_t* launches);
 
 /* ------------------------------------------------------------------------
+ * A layer split by kv head over the GPUs of one node (NVLink peers), with the
+ * output gather fused into the attention kernel.  No counterpart in the
+ * reference, which runs on one GPU; this replaces an all-gather of the
+ * layer's output after tree attention.
+ *
+ * Every rank allocates a buffer of the same size with
+ * gorgon_peer_buffer_alloc (device memory of the current device, zeroed), passes the
+ * 64-byte handle to the other ranks (any host channel), and opens theirs with
+ * gorgon_peer_buffer_open.  Each buffer holds the layer's output (the same
+ * layout on every rank) and, at signal_offset, four zeroed uint64 words of
+ * signal state.  A gorgon_peer_group lists every rank's buffer
+ * as seen from this rank (base[rank] is this rank's own).
+ *
+ * gorgon_tree_attn_gather runs gorgon_tree_attn with p->out pointing into
+ * base[rank].  The tensor-core kernel's epilogue writes each output row there
+ * and, at the same byte offset, into every other rank's buffer (stores over
+ * NVLink).  It writes into a peer's buffer only once that peer's stream has
+ * reached the same call, so the peer's earlier readers of the buffer are done.
+ * A one-CTA kernel then waits on the stream, without the host, until every
+ * peer's rows have landed here.  All ranks
+ * must make the same calls with the same shapes, in the same order.  The
+ * counters only grow, so the calls can be captured in a CUDA graph and
+ * replayed.  Every wait is bounded (gorgon_set_wait_limit_ns).  A wait that
+ * runs out (a peer that never calls) raises bit 4 of the device error word.
+ * The outputs are then incomplete and the group must be rebuilt.
+ * Needs the tcgen05 single-CTA kernel, bf16/f16 output rows of whole
+ * 16-byte chunks, and a plan without a separate merge launch (whole units
+ * or cluster plans).  Otherwise it returns GORGON_ERR_UNSUPPORTED, and the
+ * caller gathers some other way.
+ * ---------------------------------------------------------------------- */
+#define GORGON_MAX_PEERS 8
+typedef struct {
+  unsigned char bytes[64];
+} gorgon_ipc_handle;
+
+GORGON_API int gorgon_peer_buffer_alloc(size_t bytes, void** ptr, gorgon_ipc_handle* handle);
+GORGON_API int gorgon_peer_buffer_open(const gorgon_ipc_handle* handle, void** ptr);
+GORGON_API int gorgon_peer_buffer_close(void* peer_ptr);
+GORGON_API int gorgon_peer_buffer_free(void* ptr);
+
+typedef struct {
+  int32_t world;                    /* ranks, 1 .. GORGON_MAX_PEERS */
+  int32_t rank;                     /* this rank */
+  void* base[GORGON_MAX_PEERS];     /* every rank's buffer as mapped here */
+  int64_t signal_offset;            /* byte offset of the 4 signal words (8-byte aligned) */
+} gorgon_peer_group;
+
+GORGON_API int gorgon_tree_attn_gather(const gorgon_tree_attn_params* p, const gorgon_peer_group* g,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
  * Fused tree verifier: per-row argmax over the vocabulary, draft match and
  * longest accepted path in one launch, with no host synchronisation.
  * Replaces the vectorised verifier of _verify_tree_candidates

@@ -106,6 +106,18 @@ class HeadCandidateParams(Structure):
     ]
 
 
+MAX_PEERS = 8  # GORGON_MAX_PEERS
+
+
+class IpcHandle(Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class PeerGroup(Structure):
+    _fields_ = [("world", c_int32), ("rank", c_int32), ("base", c_void_p * MAX_PEERS),
+                ("signal_offset", c_int64)]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "gorgon_abi_version": (c_int, []),
@@ -117,6 +129,12 @@ SIGNATURES = {
     "gorgon_tree_attn": (c_int, [POINTER(TreeAttnParams), c_void_p, c_size_t, c_void_p]),
     "gorgon_tree_attn_plan": (c_int, [POINTER(TreeAttnParams), POINTER(c_int32), POINTER(c_int32),
                                       POINTER(c_int32)]),
+    "gorgon_peer_buffer_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(IpcHandle)]),
+    "gorgon_peer_buffer_open": (c_int, [POINTER(IpcHandle), POINTER(c_void_p)]),
+    "gorgon_peer_buffer_close": (c_int, [c_void_p]),
+    "gorgon_peer_buffer_free": (c_int, [c_void_p]),
+    "gorgon_tree_attn_gather": (c_int, [POINTER(TreeAttnParams), POINTER(PeerGroup), c_void_p, c_size_t,
+                                        c_void_p]),
     "gorgon_verify_workspace_size": (c_size_t, [POINTER(VerifyParams)]),
     "gorgon_verify": (c_int, [POINTER(VerifyParams), c_void_p, c_size_t, c_void_p]),
     "gorgon_verify_noalloc": (c_int, [POINTER(VerifyParams), c_void_p]),

@@ -1,6 +1,7 @@
 // Library-wide C ABI pieces: error reporting, the device error word, device
 // properties.  The per-operator entry points live beside their kernels.
 #include <atomic>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -83,4 +84,49 @@ extern "C" int64_t gorgon_set_wait_limit_ns(int64_t ns) {
   const uint64_t prev = g_wait_limit_ns.load();
   if (ns > 0) g_wait_limit_ns.store(static_cast<uint64_t>(ns));
   return static_cast<int64_t>(prev);
+}
+
+// ---- peer buffers for the fused output gather (CUDA IPC between the
+// processes of one node; the mapping enables peer access over NVLink)
+static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(gorgon_ipc_handle), "IPC handle size");
+
+extern "C" int gorgon_peer_buffer_alloc(size_t bytes, void** ptr, gorgon_ipc_handle* handle) {
+  using namespace gorgon;
+  if (!ptr || !handle || bytes == 0) return set_error(GORGON_ERR_INVALID, "gorgon_peer_buffer_alloc: bad argument");
+  void* p = nullptr;
+  int rc = check_cuda(cudaMalloc(&p, bytes), "gorgon_peer_buffer_alloc: cudaMalloc");
+  if (rc) return rc;
+  rc = check_cuda(cudaMemset(p, 0, bytes), "gorgon_peer_buffer_alloc: cudaMemset");
+  if (!rc) rc = check_cuda(cudaDeviceSynchronize(), "gorgon_peer_buffer_alloc: synchronize");
+  if (!rc) {
+    cudaIpcMemHandle_t h;
+    rc = check_cuda(cudaIpcGetMemHandle(&h, p), "gorgon_peer_buffer_alloc: cudaIpcGetMemHandle");
+    if (!rc) std::memcpy(handle->bytes, &h, sizeof(h));
+  }
+  if (rc) {
+    cudaFree(p);
+    return rc;
+  }
+  *ptr = p;
+  return GORGON_OK;
+}
+
+extern "C" int gorgon_peer_buffer_open(const gorgon_ipc_handle* handle, void** ptr) {
+  using namespace gorgon;
+  if (!ptr || !handle) return set_error(GORGON_ERR_INVALID, "gorgon_peer_buffer_open: bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "gorgon_peer_buffer_open: cudaIpcOpenMemHandle");
+}
+
+extern "C" int gorgon_peer_buffer_close(void* peer_ptr) {
+  using namespace gorgon;
+  if (!peer_ptr) return GORGON_OK;
+  return check_cuda(cudaIpcCloseMemHandle(peer_ptr), "gorgon_peer_buffer_close: cudaIpcCloseMemHandle");
+}
+
+extern "C" int gorgon_peer_buffer_free(void* ptr) {
+  using namespace gorgon;
+  if (!ptr) return GORGON_OK;
+  return check_cuda(cudaFree(ptr), "gorgon_peer_buffer_free: cudaFree");
 }

@@ -71,11 +71,21 @@ __device__ __forceinline__ void ancestor_bits(const int32_t* __restrict__ par, i
   }
 }
 
+// The output gather of gorgon_tree_attn_gather: the other ranks' copies of
+// a.out (same byte offset in their buffers), their signal words and ours.
+struct PeerLaunch {
+  int npeers;
+  void* peer_out[7];
+  uint64_t* peer_sig[7];
+  uint64_t* sig;
+};
+
 // Host launchers (defined in attn_simt.cu / attn_tc.cu).
 int launch_attn_simt(const AttnArgs& a, int dtype, cudaStream_t st);
 int launch_attn_combine(const AttnArgs& a, cudaStream_t st);
 bool attn_tc_supported(const AttnArgs& a, int dtype);
-int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st);
+int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st,
+                   const PeerLaunch* peers = nullptr);
 size_t attn_tc_workspace(const AttnArgs& a);
 void attn_tc_plan(const AttnArgs& a, int32_t* splits, int32_t* launches);
 // CTA-pair kernel (attn_pair.cu): whole units only, no workspace.

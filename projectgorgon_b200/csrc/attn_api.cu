@@ -219,3 +219,43 @@ extern "C" int gorgon_tree_attn(const gorgon_tree_attn_params* p, void* workspac
   if (a.splits > 1) rc = launch_attn_combine(a, st);
   return rc;
 }
+
+extern "C" int gorgon_tree_attn_gather(const gorgon_tree_attn_params* p, const gorgon_peer_group* g,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace gorgon;
+  if (!p || !g) return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: null argument");
+  if (g->world < 1 || g->world > GORGON_MAX_PEERS || g->rank < 0 || g->rank >= g->world)
+    return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: world must be 1..8 and rank in [0, world)");
+  if (g->world == 1) return gorgon_tree_attn(p, workspace, workspace_bytes, stream);
+  if (g->signal_offset < 0 || g->signal_offset % 8 != 0)
+    return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: signal_offset must be a non-negative multiple of 8");
+  for (int r = 0; r < g->world; ++r)
+    if (!g->base[r]) return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: a rank's buffer is null");
+  const char* own = static_cast<const char*>(g->base[g->rank]);
+  const char* out = static_cast<const char*>(p->out);
+  if (out < own) return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: out does not point into this rank's buffer");
+  const int64_t off = out - own;
+  AttnArgs a;
+  int rc = make_args(p, &a);
+  if (rc) return rc;
+  if (static_cast<int64_t>(a.batch) * a.hq * a.n * a.d == 0) return GORGON_OK;
+  if (choose(p, a) != Kernel::kTcCta)
+    return set_error(GORGON_ERR_UNSUPPORTED, "gorgon_tree_attn_gather: the fused gather runs on the tcgen05 "
+                                             "single-CTA kernel (bf16/f16, head_dim 128, a tree mask)");
+  const size_t need = attn_tc_workspace(a);
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return set_error(GORGON_ERR_WORKSPACE, "gorgon_tree_attn_gather: workspace smaller than gorgon_tree_attn_workspace_size()");
+  PeerLaunch pl{};
+  for (int r = 0; r < g->world; ++r) {
+    char* b = static_cast<char*>(g->base[r]);
+    uint64_t* sig = reinterpret_cast<uint64_t*>(b + g->signal_offset);
+    if (r == g->rank) {
+      pl.sig = sig;
+    } else {
+      pl.peer_out[pl.npeers] = b + off;
+      pl.peer_sig[pl.npeers] = sig;
+      ++pl.npeers;
+    }
+  }
+  return launch_attn_tc(a, p->dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), &pl);
+}

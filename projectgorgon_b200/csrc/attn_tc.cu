@@ -65,6 +65,7 @@ namespace {
 using namespace sm100;
 
 constexpr uint32_t kOffQ = 0;                          // [mtile][half]
+constexpr int kMaxPeers = 8;                           // GORGON_MAX_PEERS
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0;    // + (buf * MT + mtile) * BN
 constexpr uint32_t kColO = 256;  // + mtile * 128
@@ -103,6 +104,14 @@ struct TcArgs {
   int pair_align;     // whole units per CTA, strided by the grid (no partials to merge)
   int cluster;        // > 1: each unit cut between the CTAs of a cluster of this size, merged in DSMEM
   int q_tma;          // Q M-tiles come by TMA (tree size divides 128 or is a multiple of it)
+  // Output gather over NVLink (gorgon_tree_attn_gather): every output chunk
+  // is also stored at peer_out[p] + (its offset from a.out), for npeers
+  // other ranks; sig / peer_sig are the ranks' signal words
+  // {arrived, done, calls completed, done expected}.
+  int npeers;
+  void* peer_out[kMaxPeers - 1];
+  uint64_t* peer_sig[kMaxPeers - 1];
+  uint64_t* sig;
   int ab_fmt;         // 0 f16, 1 bf16
   int out_vec;        // 16-byte aligned output rows: kOutBf16 / kOutF16 / kOutF32, else 0
   float* part_o;      // [grid * 2][rows per unit][128]
@@ -205,6 +214,35 @@ struct Segments {
     return true;
   }
 };
+
+// ------------------------------------------------------------ output gather
+// True once every peer's stream has reached this call (each adds 1 to our
+// `arrived` word when its kernel starts, after the earlier work on its
+// stream), so their buffers are free for this call's rows; false, with the
+// timeout bit raised, if that wait runs out.
+__device__ bool peers_ready(const TcArgs& t) {
+  const uint64_t calls = *reinterpret_cast<volatile const uint64_t*>(t.sig + 2);
+  const uint64_t need = (calls + 1) * static_cast<uint64_t>(t.npeers);
+  if (ld_acquire_sys(t.sig) >= need) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(t.sig) < need) {
+    if (globaltimer_ns() - t0 > t.wait_ns) {
+      raise_device_error(t.a.err, kErrTimeout);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
+// The warp's verdict (lane 0 waits); the warp barrier orders the lanes'
+// stores to the peers after lane 0's acquire.
+__device__ __forceinline__ bool warp_peers_ready(const TcArgs& t) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = peers_ready(t) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
+}
 
 // ------------------------------------------------------------ roles
 // Streams one operand (K when is_v == 0, else V) of every tile of the CTA's
@@ -713,16 +751,32 @@ __device__ void softmax_epilogue(const TcArgs& t, uint8_t* smem, Barriers<MT>* b
         }
       }
       __syncwarp();
-      uint16_t* ob16 = static_cast<uint16_t*>(a.out) + static_cast<int64_t>(pi.b) * a.o_sb +
-                       static_cast<int64_t>(pi.kvh) * a.group * a.o_sh;
+      const int64_t ob0 = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(pi.kvh) * a.group * a.o_sh;
+      uint16_t* ob16 = static_cast<uint16_t*>(a.out) + ob0;
       RowCursor rc(prow0, a.n);
+      if (t.npeers == 0) {
 #pragma unroll 4
-      for (int k = 0; k < 16; ++k) {
-        const uint4 v = *reinterpret_cast<const uint4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
-        if (rc.pr < R)
-          *reinterpret_cast<uint4*>(ob16 + static_cast<int64_t>(rc.gq) * a.o_sh + static_cast<int64_t>(rc.node) * a.o_sn +
-                                    jc * 8) = v;
-        rc.next2(a.n);
+        for (int k = 0; k < 16; ++k) {
+          const uint4 v = *reinterpret_cast<const uint4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
+          if (rc.pr < R)
+            *reinterpret_cast<uint4*>(ob16 + static_cast<int64_t>(rc.gq) * a.o_sh +
+                                      static_cast<int64_t>(rc.node) * a.o_sn + jc * 8) = v;
+          rc.next2(a.n);
+        }
+      } else {
+        // the same rows into every peer's buffer too, once the peers are ready
+        const int np = warp_peers_ready(t) ? t.npeers : 0;
+#pragma unroll 1
+        for (int k = 0; k < 16; ++k) {
+          const uint4 v = *reinterpret_cast<const uint4*>(stage_at(q_tile, wq, sub + 2 * k, jc));
+          if (rc.pr < R) {
+            const int64_t off = static_cast<int64_t>(rc.gq) * a.o_sh + static_cast<int64_t>(rc.node) * a.o_sn + jc * 8;
+            *reinterpret_cast<uint4*>(ob16 + off) = v;
+            for (int p = 0; p < np; ++p)
+              *reinterpret_cast<uint4*>(static_cast<uint16_t*>(t.peer_out[p]) + ob0 + off) = v;
+          }
+          rc.next2(a.n);
+        }
       }
       __syncwarp();
     } else if (mode == kOutF32) {
@@ -834,6 +888,9 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // (output gather) this rank's stream has reached the call: peers may write here
+  if (t.npeers && blockIdx.x == 0 && threadIdx.x == 0)
+    for (int p = 0; p < t.npeers; ++p) red_add_release_sys(t.peer_sig[p], 1);
 
   int64_t g0 = 0, g1 = 0;
   bool work;
@@ -877,6 +934,14 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     __syncwarp();
     cluster_sync();   // every piece of the cluster's unit is in the workspace
     cluster_merge<MT>(t);
+  }
+  if (t.npeers) {
+    // (output gather) one count per CTA in every peer's `done` word, after
+    // the CTA barrier: the release is cumulative, so it orders every
+    // thread's stores to the peers that the barrier ordered before it
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int p = 0; p < t.npeers; ++p) red_add_release_sys(t.peer_sig[p] + 1, 1);
   }
   if (bars->abort && threadIdx.x == 0) raise_device_error(t.a.err, kErrTimeout);
   if (warp == 2) {
@@ -926,10 +991,15 @@ __device__ __forceinline__ float warp_max(float x) {
 }
 
 // Writes four consecutive output columns of one row.
-__device__ __forceinline__ void store4(const TcArgs& t, int64_t idx, float x, float y, float z, float w) {
+// np: peers whose buffers also get the values (the output gather; 16-bit
+// outputs only, and only after warp_peers_ready).
+__device__ __forceinline__ void store4(const TcArgs& t, int64_t idx, float x, float y, float z, float w,
+                                       int np = 0) {
   if (t.out_vec == kOutBf16 || t.out_vec == kOutF16) {
     const bool bf = t.out_vec == kOutBf16;
-    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(t.a.out) + idx) = make_uint2(pack16x2(x, y, bf), pack16x2(z, w, bf));
+    const uint2 v = make_uint2(pack16x2(x, y, bf), pack16x2(z, w, bf));
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(t.a.out) + idx) = v;
+    for (int p = 0; p < np; ++p) *reinterpret_cast<uint2*>(static_cast<uint16_t*>(t.peer_out[p]) + idx) = v;
   } else if (t.out_vec == kOutF32) {
     *reinterpret_cast<float4*>(static_cast<float*>(t.a.out) + idx) = make_float4(x, y, z, w);
   } else {
@@ -970,6 +1040,7 @@ __device__ void cluster_merge_n(const TcArgs& t) {
   // this CTA's rows that are real packed rows: [r0, r1)
   const int r0 = c * C::kQRows / NC;
   const int r1 = min((c + 1) * C::kQRows / NC, R - pi.qg * C::kQRows);
+  const int np = (t.npeers && r0 + warp < r1 && warp_peers_ready(t)) ? t.npeers : 0;
 #pragma unroll 1
   for (int rb = r0 + warp; rb < r1; rb += kWarps * kRows) {
     // lane k * NC + j holds piece j's log-sum-exp of batch row k (-inf for a
@@ -1024,11 +1095,11 @@ __device__ void cluster_merge_n(const TcArgs& t) {
       const int64_t ob = static_cast<int64_t>(pi.b) * a.o_sb + static_cast<int64_t>(h) * a.o_sh +
                          static_cast<int64_t>(node) * a.o_sn;
       if (M == -INFINITY) {
-        store4(t, ob + lane * 4, NAN, NAN, NAN, NAN);
+        store4(t, ob + lane * 4, NAN, NAN, NAN, NAN, np);
         if (a.lse && lane == 0) a.lse[orow] = -INFINITY;
       } else {
         const float winv = 1.f / wsum;
-        store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv);
+        store4(t, ob + lane * 4, acc.x * winv, acc.y * winv, acc.z * winv, acc.w * winv, np);
         if (a.lse && lane == 0) a.lse[orow] = (M + __log2f(wsum)) * 0.6931471805599453f;
       }
     }
@@ -1174,6 +1245,24 @@ __global__ void __launch_bounds__(kCombineThreads) attn_tc_combine(const TcArgs 
     }
     finish(k, M, wsum, acc);
   }
+}
+
+// (output gather) Ends the call on this rank's stream: waits until every
+// peer CTA of the call has counted in our `done` word (a running total:
+// npeers x grid more than after the last call), then records the call.
+__global__ void attn_peer_wait(uint64_t* sig, int npeers, int grid, uint64_t wait_ns, uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  const uint64_t expected = sig[3] + static_cast<uint64_t>(npeers) * static_cast<uint64_t>(grid);
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys(sig + 1) < expected) {
+    if (globaltimer_ns() - t0 > wait_ns) {
+      raise_device_error(err, kErrTimeout);
+      break;
+    }
+    __nanosleep(100);
+  }
+  sig[3] = expected;
+  sig[2] = sig[2] + 1;
 }
 
 // ------------------------------------------------------------ host side
@@ -1428,11 +1517,15 @@ void attn_tc_plan(const AttnArgs& a, int32_t* splits, int32_t* launches) {
   *launches = 1 + (pl.varlen ? 1 : 0) + (pl.pair_align || pl.cluster ? 0 : 1);
 }
 
-int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st) {
+int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_bytes, cudaStream_t st,
+                   const PeerLaunch* peers) {
   const Plan pl = make_plan(a);
   const WsLayout w = ws_layout(pl);
   if (!workspace || ws_bytes < w.total)
     return set_error(GORGON_ERR_WORKSPACE, "tcgen05 tree attention: workspace too small");
+  if (peers && !pl.pair_align && !pl.cluster)
+    return set_error(GORGON_ERR_UNSUPPORTED, "tree attention gather: this shape's plan merges pieces in a second "
+                                             "launch (stream-K); the fused gather needs whole units or a cluster plan");
   EncodeTiledFn enc = encode_fn();
   if (!enc) return set_error(GORGON_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
   const CUtensorMapDataType tdt = dtype == GORGON_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1507,8 +1600,21 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
   }
-  return pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, qmap, t, st)
-                    : launch_mt<2>(a, dtype, pl, kmap, vmap, qmap, t, st);
+  if (peers) {
+    if (t.out_vec != kOutBf16 && t.out_vec != kOutF16)
+      return set_error(GORGON_ERR_UNSUPPORTED, "tree attention gather: needs bf16/f16 output rows of whole 16-byte chunks");
+    t.npeers = peers->npeers;
+    for (int p = 0; p < peers->npeers; ++p) {
+      t.peer_out[p] = peers->peer_out[p];
+      t.peer_sig[p] = peers->peer_sig[p];
+    }
+    t.sig = peers->sig;
+  }
+  const int rc = pl.mt == 1 ? launch_mt<1>(a, dtype, pl, kmap, vmap, qmap, t, st)
+                            : launch_mt<2>(a, dtype, pl, kmap, vmap, qmap, t, st);
+  if (rc || !peers) return rc;
+  attn_peer_wait<<<1, 32, 0, st>>>(peers->sig, peers->npeers, pl.grid, t.wait_ns, a.err);
+  return check_cuda(cudaGetLastError(), "tree attention gather: wait launch");
 }
 
 }  // namespace gorgon

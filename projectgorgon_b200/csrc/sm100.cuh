@@ -128,19 +128,14 @@ __device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t p
 __device__ __forceinline__ void st_cluster_u32(uint32_t addr_cluster, uint32_t v) {
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr_cluster), "r"(v) : "memory");
 }
-// Loads from any CTA of the cluster (a shared::cluster address).  No memory
-// clobber, so that a run of them issues back to back; the cluster barrier
-// that makes the data visible is itself a compiler barrier.
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr_cluster) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr_cluster));
-  return v;
+// System-scope signalling between GPUs (NVLink peers): a release add to a
+// counter in another GPU's memory, and an acquire load of one's own.
+__device__ __forceinline__ void red_add_release_sys(uint64_t* addr, uint64_t v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
-__device__ __forceinline__ float4 ld_cluster_v4(uint32_t addr_cluster) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr_cluster));
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* addr) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
   return v;
 }
 

@@ -60,6 +60,7 @@ def tree_attention(
     backend: str = "auto",
     num_splits: int = 0,
     out: Optional[torch.Tensor] = None,
+    peer_group=None,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Masked softmax attention of tree queries over prefix + tree keys.
 
@@ -68,7 +69,11 @@ def tree_attention(
     ``return_lse`` also the natural-log sum-exp ``[B, Hq, N]`` (float32).
     ``out``, when given, is written instead of a new tensor: 4-D ``q`` only,
     shape ``[B, Hq, N, D]``, any strides with ``head_dim`` contiguous (e.g. a
-    head-major slice of a larger buffer).
+    head-major slice of a larger buffer).  ``peer_group`` (a
+    ``sharding.PeerHeadOutput``, with ``out`` its ``local`` view) also writes
+    the rows into every other rank's copy of the buffer from the kernel's
+    epilogue and waits on the stream until the other ranks' rows have landed
+    here (``gorgon_tree_attn_gather``).
     """
     prep = _prepare(q, k, v, tree_mask, parents, max_depth, cu_seqlens, max_seqlen, scale,
                     out_dtype, return_lse, backend, num_splits, out)
@@ -77,7 +82,11 @@ def tree_attention(
     with on_device(dev):
         nbytes = lib.gorgon_tree_attn_workspace_size(prep.p)
         ws = workspace(nbytes, dev) if nbytes else None
-        _abi.check(lib.gorgon_tree_attn(prep.p, ptr(ws), nbytes, stream_ptr(dev)), "gorgon_tree_attn")
+        if peer_group is None:
+            _abi.check(lib.gorgon_tree_attn(prep.p, ptr(ws), nbytes, stream_ptr(dev)), "gorgon_tree_attn")
+        else:
+            _abi.check(lib.gorgon_tree_attn_gather(prep.p, peer_group.group_ref(), ptr(ws), nbytes,
+                                                   stream_ptr(dev)), "gorgon_tree_attn_gather")
     out = prep.out
     if q.dim() != 4:
         out = out.reshape(tuple(q.shape[:-1]) + (out.shape[-1],))

@@ -17,6 +17,7 @@ max-over-ranks timing and the gathers.
 """
 from __future__ import annotations
 
+import ctypes
 import datetime
 import os
 from dataclasses import dataclass
@@ -151,6 +152,97 @@ def gather_heads_inplace(full: torch.Tensor, async_op: bool = False):
             work = dist.all_gather(list(flat.view(world, chunk).unbind(0)), mine.clone(), async_op=async_op)
     view = full.permute(1, 0, 2, 3)
     return (view, work) if async_op else view
+
+
+class _DeviceArray:
+    """A raw device allocation described by the CUDA array interface (so
+    torch can view it without owning it)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (nbytes,), "typestr": "|u1",
+                                         "version": 3, "strides": None}
+
+
+class PeerHeadOutput:
+    """The head-major layer output ``[Hq, B, N, D]`` of a layer split by kv
+    head, with the gather fused into the attention kernel.
+
+    Every rank allocates its buffer with ``gorgon_peer_buffer_alloc``, the
+    handles go round the process group (any backend; only bytes on the host),
+    and each rank maps the others' buffers (CUDA IPC; the kernels reach them
+    over NVLink).  ``tree_attention(..., out=self.local, peer_group=self)``
+    then writes this rank's query heads into every rank's buffer from the
+    kernel's epilogue and waits on the stream for the other ranks' heads: no
+    all-gather call, the transfer overlapping the attention tile by tile.
+    ``full`` is this rank's buffer as ``[B, Hq, N, D]`` (head-major strides),
+    ``local`` the ``[B, Hq / world, N, D]`` part this rank computes.  Call
+    :meth:`close` on every rank (it synchronises them) before the process
+    group goes."""
+
+    SIGNAL_BYTES = 256  # four uint64 signal words, padded
+
+    def __init__(self, batch: int, heads_q: int, heads_kv: int, n: int, d: int, dtype: torch.dtype,
+                 device: torch.device, world: int, rank: int, group=None):
+        from . import _abi
+        (_, _), (q0, q1) = shard_heads(heads_kv, heads_q, world, rank)
+        if q1 - q0 != heads_q // world:
+            raise ValueError(f"{heads_q} query heads do not split evenly over {world} ranks")
+        self.world, self.rank, self.group = world, rank, group
+        esz = torch.tensor([], dtype=dtype).element_size()
+        data = heads_q * batch * n * d * esz
+        self.signal_offset = (data + 255) // 256 * 256
+        nbytes = self.signal_offset + self.SIGNAL_BYTES
+        lib = _abi.lib()
+        own, handle = ctypes.c_void_p(), _abi.IpcHandle()
+        with torch.cuda.device(device):
+            _abi.check(lib.gorgon_peer_buffer_alloc(nbytes, ctypes.byref(own), ctypes.byref(handle)),
+                       "gorgon_peer_buffer_alloc")
+            self._own = own.value
+            self._opened: List[int] = []
+            handles = [bytes(handle.bytes)]
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, bytes(handle.bytes), group=group)
+            bases = []
+            for r in range(world):
+                if r == rank:
+                    bases.append(self._own)
+                    continue
+                h = _abi.IpcHandle()
+                ctypes.memmove(h.bytes, handles[r], 64)
+                p = ctypes.c_void_p()
+                _abi.check(lib.gorgon_peer_buffer_open(ctypes.byref(h), ctypes.byref(p)), "gorgon_peer_buffer_open")
+                self._opened.append(p.value)
+                bases.append(p.value)
+        base_arr = (ctypes.c_void_p * _abi.MAX_PEERS)(*bases)
+        self._group = _abi.PeerGroup(world, rank, base_arr, self.signal_offset)
+        raw = torch.as_tensor(_DeviceArray(self._own, nbytes), device=device)
+        self._raw = raw
+        self.full_head_major = raw[:data].view(dtype).view(heads_q, batch, n, d)
+        self.full = self.full_head_major.permute(1, 0, 2, 3)
+        self.local = self.full_head_major[q0:q1].permute(1, 0, 2, 3)
+
+    def group_ref(self):
+        return ctypes.byref(self._group)
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buffers and frees this rank's, after every
+        rank has stopped using them (a barrier on the group)."""
+        from . import _abi
+        if self._own is None:
+            return
+        lib = _abi.lib()
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            lib.gorgon_peer_buffer_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self._raw = self.full_head_major = self.full = self.local = None
+        lib.gorgon_peer_buffer_free(ctypes.c_void_p(self._own))
+        self._own = None
 
 
 def max_over_ranks(value: float, device: torch.device = None) -> float:
