@@ -417,6 +417,11 @@ class HeadShardWorkload(Workload):
         return sharding.gather_heads(o)
 
     @property
+    def lockstep(self) -> bool:
+        """With the fused gather each step waits for the other ranks' rows."""
+        return self.gather == "fused" and self.world > 1
+
+    @property
     def persistent_out(self) -> bool:
         """End-to-end steps write the peer buffers (``e2e_step``), not a fresh tensor."""
         return self.gather == "fused"
@@ -1086,6 +1091,12 @@ def time_device(wl: Workload, steps: int, warmup: int, world: int, graph: bool =
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     with ClockSampler(dev) as clk:
+        if getattr(wl, "lockstep", False):
+            # ranks whose steps wait on one another on the device: one more
+            # untimed step queued right before the timed ones, so that every
+            # rank's timed region starts when that step's handshake releases
+            # it, not when its host left the barrier
+            step()
         for i in range(steps):
             if flush is not None:
                 flush.fill_(i & 0xff)
@@ -1233,6 +1244,8 @@ def time_e2e(wl: Workload, steps: int, warmup: int, world: int):
     torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
+    if getattr(wl, "lockstep", False):
+        wl.step()  # untimed: the ranks leave this step's handshake together (see time_device)
     e0, e1 = ev(), ev()
     e0.record(s_c)
     s_in.wait_event(e0)
