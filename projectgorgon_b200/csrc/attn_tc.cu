@@ -117,6 +117,7 @@ struct TcArgs {
   float* part_o;      // [grid * 2][rows per unit][128]
   float* part_lse;    // [grid * 2][rows per unit]
   int* tile_start;    // varlen: [units + 1] tile prefix (written by attn_tc_prologue)
+  int* order;         // varlen whole units: unit ids, most tiles first (attn_tc_prologue_sorted); else null
   uint64_t wait_ns;   // bound on every wait (wait_limit_ns())
 };
 
@@ -191,20 +192,32 @@ __device__ __forceinline__ PairInfo pair_info(const TcArgs& t, int p) {
 // [g0, g1) (stream-K).
 struct Segments {
   int64_t g0, g1;
-  int unit;
+  int unit, round = 0;
   __device__ Segments(int64_t r0, int64_t r1) : g0(r0), g1(r1), unit(blockIdx.x) {}
   __device__ bool next(const TcArgs& t, int64_t& g, int64_t& e, PairInfo& pi) {
     if (t.pair_align) {
-      while (unit < t.pairs) {
-        pi = pair_info(t, unit);
-        unit += t.grid;
+      while (true) {
+        int u;
+        if (t.order) {
+          // units sorted by tile count, dealt out in snake order: CTA c takes
+          // sorted unit c in round 0, grid - 1 - c in round 1, and so on
+          const int i = round * t.grid + ((round & 1) ? t.grid - 1 - static_cast<int>(blockIdx.x)
+                                                      : static_cast<int>(blockIdx.x));
+          if (i >= t.pairs) return false;
+          u = t.order[i];
+          ++round;
+        } else {
+          if (unit >= t.pairs) return false;
+          u = unit;
+          unit += t.grid;
+        }
+        pi = pair_info(t, u);
         if (pi.end > pi.start) {
           g = pi.start;
           e = pi.end;
           return true;
         }
       }
-      return false;
     }
     if (g0 >= g1) return false;
     pi = pair_info(t, pair_of(t, g0));
@@ -234,7 +247,7 @@ __device__ bool peers_ready(const TcArgs& t) {
   }
   return true;
 }
-// The warp's verdict (lane 0 waits); the warp barrier orders the lanes'
+// The warp's answer (lane 0 waits); the warp barrier orders the lanes'
 // stores to the peers after lane 0's acquire.
 __device__ __forceinline__ bool warp_peers_ready(const TcArgs& t) {
   int ok = 1;
@@ -968,6 +981,41 @@ __global__ void attn_tc_prologue(const TcArgs t) {
   t.tile_start[p] = acc;
 }
 
+// Varlen schedule for whole units (one CTA of 1024 threads, at most
+// kMaxSortedUnits units): the tile prefix as above, and the unit ids ordered
+// by tile count, most first (ties by id), for the snake deal of Segments.
+constexpr int kMaxSortedUnits = 1024;
+template <int MT>
+__global__ void __launch_bounds__(1024) attn_tc_prologue_sorted(const TcArgs t) {
+  constexpr int kBN = Cfg<MT>::kBN;
+  __shared__ int cnt[kMaxSortedUnits];
+  const int U = t.pairs;
+  const int per_b = t.a.hkv * t.qgroups;
+  for (int u = threadIdx.x; u < U; u += blockDim.x) {
+    const int b = u / per_b;
+    const int L = t.a.cu_seqlens[b + 1] - t.a.cu_seqlens[b];
+    cnt[u] = L > 0 ? (L + kBN - 1) / kBN : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int u = 0; u < U; ++u) {
+      t.tile_start[u] = acc;
+      acc += cnt[u];
+    }
+    t.tile_start[U] = acc;
+  }
+  for (int u = threadIdx.x; u < U; u += blockDim.x) {
+    const int c = cnt[u];
+    int r = 0;
+    for (int v = 0; v < U; ++v) {
+      const int cv = cnt[v];
+      r += (cv > c || (cv == c && v < u)) ? 1 : 0;
+    }
+    t.order[r] = u;
+  }
+}
+
 // Merges the pieces of every unit that the stream-K schedule cut between
 // CTAs: out = sum_k 2^(lse_k - M) o_k / sum_k 2^(lse_k - M) with M = max_k
 // lse_k (log2 units) and o_k each piece's normalised output.  Grid (units,
@@ -1288,6 +1336,7 @@ struct Plan {
   int qgroups, pairs, tiles_per_pair, grid;
   bool varlen, pair_align;
   int cluster;  // > 1: CTAs per unit in a thread-block cluster (no workspace partials, no merge launch)
+  bool sorted;  // varlen whole units, longest first (attn_tc_prologue_sorted)
 };
 
 template <int MT>
@@ -1318,6 +1367,12 @@ Plan make_plan_mt(const AttnArgs& a) {
   if (pl.varlen) {
     pl.tiles_per_pair = 0;
     pl.grid = a.splits > 0 ? a.splits : sms;
+    if (a.splits <= 0 && pl.pairs >= sms && pl.pairs <= kMaxSortedUnits) {
+      // enough units to fill the GPU: whole units, longest first, dealt out
+      // in snake order (no partials, no merge launch)
+      pl.pair_align = true;
+      pl.sorted = true;
+    }
   } else {
     pl.tiles_per_pair = (a.kv_len + C::kBN - 1) / C::kBN;
     const int64_t T = static_cast<int64_t>(pl.pairs) * pl.tiles_per_pair;
@@ -1380,7 +1435,7 @@ constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t part_o, part_lse, tile_start, total;
+  size_t part_o, part_lse, tile_start, order, total;
 };
 
 WsLayout ws_layout(const Plan& pl) {
@@ -1388,6 +1443,7 @@ WsLayout ws_layout(const Plan& pl) {
   WsLayout w{};
   size_t off = 0;
   w.tile_start = off; off += align_up(static_cast<size_t>(pl.pairs + 1) * sizeof(int));
+  w.order = off;      off += align_up(static_cast<size_t>(pl.sorted ? pl.pairs : 0) * sizeof(int));
   const size_t slots = static_cast<size_t>(pl.grid) * 2;
   w.part_lse = off;   off += align_up(slots * rows * sizeof(float));
   w.part_o = off;     off += align_up(slots * rows * kD * sizeof(float));
@@ -1459,7 +1515,10 @@ int launch_mt(const AttnArgs& a, int dtype, const Plan& pl, const CUtensorMap& k
   using C = Cfg<MT>;
   int rc = GORGON_OK;
   if (pl.varlen) {
-    attn_tc_prologue<MT><<<1, 32, 0, st>>>(t);
+    if (pl.sorted)
+      attn_tc_prologue_sorted<MT><<<1, 1024, 0, st>>>(t);
+    else
+      attn_tc_prologue<MT><<<1, 32, 0, st>>>(t);
     rc = check_cuda(cudaGetLastError(), "tcgen05 prologue launch");
     if (rc) return rc;
   }
@@ -1570,6 +1629,7 @@ int launch_attn_tc(const AttnArgs& a, int dtype, void* workspace, size_t ws_byte
   t.wait_ns = wait_limit_ns();
   char* ws = static_cast<char*>(workspace);
   t.tile_start = reinterpret_cast<int*>(ws + w.tile_start);
+  t.order = pl.sorted ? reinterpret_cast<int*>(ws + w.order) : nullptr;
   t.part_lse = reinterpret_cast<float*>(ws + w.part_lse);
   t.part_o = reinterpret_cast<float*>(ws + w.part_o);
   {
