@@ -49,10 +49,10 @@ from projectgorgon_b200.trees import best_first_tree, cartesian_tree, random_tre
 # dominant kernel from the ncu captures summarised under profiles/, keyed by
 # (workload, backend).  None until a capture exists.
 NCU_TRAFFIC_BYTES = {
-    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.551 MB read + 4.671 MB written
-    ("verify-b16-p8192-n64", "tcgen05"): 554221568,
-    # profiles/attn_tc_kernel_verify-b1-p2048-n64.md: 9.273 MB read, 0 written
-    ("verify-b1-p2048-n64", "tcgen05"): 9273088,
+    # profiles/attn_tc_kernel_verify-b16-p8192-n64.md: 549.566 MB read + 3.622 MB written
+    ("verify-b16-p8192-n64", "tcgen05"): 553188096,
+    # profiles/attn_tc_kernel_verify-b1-p2048-n64.md (cluster plan): 9.296 MB read, 0 written
+    ("verify-b1-p2048-n64", "tcgen05"): 9295616,
     # profiles/verify_kernel_verifier-b32-n64-v128256.md: 570.646 MB read + 4.049 MB written
     ("verifier-b32-n64-v128256", "verify_kernel"): 574694912,
     # profiles/kv_trim_warp_kernel_kvtrim-b32-l32-p4096.md: the 4-layer capture (1.389 MB read,
