@@ -249,3 +249,32 @@ def test_cluster_row_that_sees_nothing_is_nan():
     keep = [i for i in range(N) if i != 5]
     ref = O.tree_attention_batched(_np(q), _np(k), _np(v), mask=_np(m).astype(bool))
     np.testing.assert_allclose(o[:, :, keep], ref[:, :, keep], atol=ATOL, rtol=RTOL)
+
+
+def test_ragged_sorted_whole_units_match_oracle():
+    """A ragged batch with more one-M-tile units than SMs (12 sequences x 8
+    kv heads x 2 = 192): whole units ranked by tile count on the device and
+    dealt out longest first, two launches (the schedule kernel and the
+    attention), no merge kernel; every sequence against the oracle."""
+    rng = random.Random(31)
+    B, Hq, Hkv, N, D = 12, 32, 8, 64, 128
+    Ls = [rng.randint(16, 3000) + N for _ in range(B)]
+    cu = np.concatenate([[0], np.cumsum(Ls)]).astype(np.int32)
+    pars = _trees(B, N, seed=31)
+    g = torch.Generator(device="cuda").manual_seed(31)
+    s = 1 / math.sqrt(D)
+    q = (torch.randn(B, Hq, N, D, device="cuda", generator=g) * s).bfloat16()
+    kp = (torch.randn(int(cu[-1]), Hkv, D, device="cuda", generator=g) * s).bfloat16()
+    vp = (torch.randn(int(cu[-1]), Hkv, D, device="cuda", generator=g) * s).bfloat16()
+    kw = dict(parents=torch.tensor(pars, device="cuda"), max_depth=5,
+              cu_seqlens=torch.from_numpy(cu).cuda(), max_seqlen=max(Ls))
+    plan = G.tree_attention_plan(q, kp, vp, **kw, backend="tcgen05")
+    assert plan["backend"] == "tcgen05" and plan["launches"] == 2
+    out, lse = G.tree_attention(q, kp, vp, **kw, backend="tcgen05", return_lse=True)
+    _, lse_s = G.tree_attention(q, kp, vp, **kw, backend="simt", return_lse=True)
+    np.testing.assert_allclose(_np(lse), _np(lse_s), atol=2e-3, rtol=1e-4)
+    for b in range(B):
+        kb = _np(kp[cu[b]:cu[b + 1]]).transpose(1, 0, 2)[None]
+        vb = _np(vp[cu[b]:cu[b + 1]]).transpose(1, 0, 2)[None]
+        ref = O.tree_attention_batched(_np(q[b:b + 1]), kb, vb, parents=pars[b], max_depth=5)
+        np.testing.assert_allclose(_np(out[b:b + 1]), ref, atol=ATOL, rtol=RTOL)
