@@ -473,6 +473,7 @@ class VerifyWorkload:
     length occur."""
 
     metric = "tree verifier HBM GB/s (logits bytes / step time)"
+    graphable = True  # one stream-ordered public call, no host sync
     data = "synthetic (seeded N(0,2) bf16 logits, random trees, drafts 1/4 on argmax paths)"
     bound = "hbm"
 
@@ -584,6 +585,8 @@ class TrimWorkload:
     right after the prefix, in place, in one launch over all layers."""
 
     metric = "KV trim HBM GB/s (rows moved, read + write, / step time)"
+    graphable = True  # one stream-ordered public call (the layer pointers go by value)
+    flush_l2 = True  # the ~22 MB of rows a step moves fit in L2
     data = "synthetic (seeded N(0,1) bf16 caches, random trees, random accepted paths)"
     bound = "hbm"
 
@@ -694,6 +697,7 @@ class CandidateWorkload:
     under the node budget."""
 
     metric = "candidate-tree builder HBM GB/s (logits bytes / step time)"
+    graphable = True  # stream-ordered public call: three launches, workspace from torch's allocator
     data = "synthetic (seeded N(0,2) bf16 head logits)"
     bound = "hbm"
     flush_l2 = True  # 33 MB of logits fit in L2
@@ -777,6 +781,7 @@ class HeadsWorkload:
     larger than L2, so no flush is needed between steps."""
 
     metric = "fused Medusa heads HBM GB/s (lm_head weight bytes / step time)"
+    graphable = True  # stream-ordered public call (the weight pointers go by value)
     data = "synthetic (seeded N(0, 0.02) bf16 lm_head weights, N(0, 1) bf16 head inputs)"
     bound = "hbm"
     flush_l2 = False
