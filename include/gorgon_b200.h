@@ -203,7 +203,8 @@ typedef struct {
   int32_t world;                    /* ranks, 1 .. GORGON_MAX_PEERS */
   int32_t rank;                     /* this rank */
   void* base[GORGON_MAX_PEERS];     /* every rank's buffer as mapped here */
-  int64_t signal_offset;            /* byte offset of the 4 signal words (8-byte aligned) */
+  int64_t signal_offset;            /* byte offset of the 4 signal words (8-byte aligned); the
+                                       output must lie wholly before it, or the call is refused */
 } gorgon_peer_group;
 
 GORGON_API int gorgon_tree_attn_gather(const gorgon_tree_attn_params* p, const gorgon_peer_group* g,

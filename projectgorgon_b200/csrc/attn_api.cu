@@ -235,6 +235,18 @@ extern "C" int gorgon_tree_attn_gather(const gorgon_tree_attn_params* p, const g
   const char* out = static_cast<const char*>(p->out);
   if (out < own) return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: out does not point into this rank's buffer");
   const int64_t off = out - own;
+  {
+    // every output element (and so its copy in each peer's buffer) must lie
+    // in the data region, before the signal words
+    const int64_t esz = p->out_dtype == GORGON_F32 ? 4 : 2;
+    if (p->o_stride_b < 0 || p->o_stride_h < 0 || p->o_stride_n < 0)
+      return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: negative output strides");
+    const int64_t last = (p->batch - 1) * p->o_stride_b + (p->heads_q - 1) * p->o_stride_h +
+                         (p->n_tree - 1) * p->o_stride_n + p->head_dim;
+    if (p->batch > 0 && p->heads_q > 0 && p->n_tree > 0 && off + last * esz > g->signal_offset)
+      return set_error(GORGON_ERR_INVALID, "gorgon_tree_attn_gather: out reaches past the buffer's data region "
+                                           "(signal_offset)");
+  }
   AttnArgs a;
   int rc = make_args(p, &a);
   if (rc) return rc;

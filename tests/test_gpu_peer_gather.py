@@ -58,6 +58,37 @@ def test_group_of_one_is_the_plain_call():
         peer.close()
 
 
+def test_gather_refuses_an_output_past_the_data_region():
+    """The fused gather writes the same offsets in every peer's buffer, so an
+    output view that runs into the signal words is refused before anything
+    launches (checked here with a two-entry group on one GPU)."""
+    import ctypes
+    import projectgorgon_b200 as G
+    from projectgorgon_b200 import _abi, sharding
+    B, Hq, Hkv, N, P = 2, 32, 8, 64, 300
+    q, k, v, pars = _layer(B, Hq, Hkv, N, P, "cuda")
+    par_t = torch.tensor(pars, device="cuda", dtype=torch.int32)
+    peer = sharding.PeerHeadOutput(B, Hq, Hkv, N, 128, torch.bfloat16, torch.device("cuda", 0), 1, 0)
+    try:
+        own = peer.full_head_major.data_ptr()
+        bases = (ctypes.c_void_p * _abi.MAX_PEERS)(own, own)
+
+        class _TwoRanks:
+            group = _abi.PeerGroup(2, 0, bases, peer.signal_offset)
+
+            def group_ref(self):
+                return ctypes.byref(self.group)
+
+        full = peer.full_head_major
+        shifted = full.as_strided(full.shape, full.stride(), full.storage_offset() + 8).permute(1, 0, 2, 3)
+        with pytest.raises(RuntimeError, match="data region"):
+            G.fused_tree_verify(q, k, v, par_t, max_depth=5, out=shifted, peer_group=_TwoRanks())
+        torch.cuda.synchronize()
+        assert G.device_error(clear=True) == 0
+    finally:
+        peer.close()
+
+
 def _free_port() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
