@@ -83,23 +83,25 @@ __global__ void __launch_bounds__(kThreads) kv_trim_kernel(const TrimArgs a) {
   }
 }
 
-// Fast path for the common case (16-byte aligned rows, at most kRegChunks * 32
-// 16-byte chunks per slice, e.g. 16 rows of 256 bytes): one warp per (layer,
-// K/V, batch row, head) slice, kWarps heads per CTA, so the whole trim of a
-// decode step is one wave of CTAs.  Lengths, destination starts and indices
-// are fetched together (indices up to max_len, unconditionally in range of the
-// index row), the slice's source rows go to registers, a warp barrier orders
-// every lane's loads before any lane's stores (in-place moves whose slots
-// overlap later sources stay correct), then the rows are written.
+// Fast path for the common case (16-byte aligned rows, at most kChunks * 32
+// 16-byte chunks per slice, e.g. 8 rows of 256 bytes with kChunks = 4): one
+// warp per (layer, batch row, head), moving both its K and its V slice, kWarps
+// heads per CTA.  Lengths, destination starts and indices are fetched once
+// for both (indices up to max_len, unconditionally in range of the index row),
+// both slices' source rows go to registers in one batch of loads, a warp
+// barrier orders every lane's loads before any lane's stores (in-place moves
+// whose slots overlap later sources stay correct), then the rows are written.
+// The register array is sized to the slice (kChunks), so short paths leave
+// room for more resident warps: the whole trim of a decode step is then one
+// wave of round trips.
 constexpr int kWarps = 8;
-constexpr int kRegChunks = 8;
 
+template <int kChunks>
 __global__ void __launch_bounds__(kWarps * 32) kv_trim_warp_kernel(const TrimArgs a, int heads) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x * kWarps + warp;
   const int b = blockIdx.y;
-  const int layer = blockIdx.z >> 1;
-  const int kv = blockIdx.z & 1;
+  const int layer = blockIdx.z;
   if (h >= heads) return;
   const int32_t* ib = a.idx + static_cast<int64_t>(b) * a.idx_sb;
   const int len = a.lens[b];
@@ -113,26 +115,34 @@ __global__ void __launch_bounds__(kWarps * 32) kv_trim_warp_kernel(const TrimArg
   }
   if (len == 0) return;
   const int64_t slice = (static_cast<int64_t>(b) * a.sb + static_cast<int64_t>(h) * a.sh) * a.elem_bytes;
-  const char* src = static_cast<const char*>(a.src[kv][layer]) + slice;
-  char* dst = static_cast<char*>(a.dst[kv][layer]) + slice;
+  const char* src0 = static_cast<const char*>(a.src[0][layer]) + slice;
+  const char* src1 = static_cast<const char*>(a.src[1][layer]) + slice;
   const int64_t rs = a.ss * a.elem_bytes;
   const int vpr = static_cast<int>(a.row_bytes / 16);
   const int total = len * vpr;
-  uint4 v[kRegChunks];
+  uint4 v0[kChunks], v1[kChunks];
 #pragma unroll
-  for (int k = 0; k < kRegChunks; ++k) {
+  for (int k = 0; k < kChunks; ++k) {
     const int e = lane + 32 * k;
     const int r = e / vpr;
     const int s = __shfl_sync(0xffffffffu, my_src, min(r, 31));  // every lane, one program point
-    if (e < total) v[k] = __ldcs(reinterpret_cast<const uint4*>(src + s * rs + (e - r * vpr) * 16));
+    if (e < total) {
+      const int64_t off = s * rs + (e - r * vpr) * 16;
+      v0[k] = __ldcs(reinterpret_cast<const uint4*>(src0 + off));
+      v1[k] = __ldcs(reinterpret_cast<const uint4*>(src1 + off));
+    }
   }
   __syncwarp();
+  char* dst0 = static_cast<char*>(a.dst[0][layer]) + slice;
+  char* dst1 = static_cast<char*>(a.dst[1][layer]) + slice;
 #pragma unroll
-  for (int k = 0; k < kRegChunks; ++k) {
+  for (int k = 0; k < kChunks; ++k) {
     const int e = lane + 32 * k;
     if (e < total) {
       const int r = e / vpr, c = e - r * vpr;
-      *reinterpret_cast<uint4*>(dst + (d0 + r) * rs + c * 16) = v[k];
+      const int64_t off = (d0 + r) * rs + c * 16;
+      *reinterpret_cast<uint4*>(dst0 + off) = v0[k];
+      *reinterpret_cast<uint4*>(dst1 + off) = v1[k];
     }
   }
 }
@@ -175,7 +185,8 @@ extern "C" int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream) {
   }
   a.vec_ok = vec;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (vec && p->max_len <= 32 && p->max_len * (row_bytes / 16) <= 32 * kRegChunks) {
+  const int64_t chunks = p->max_len * (row_bytes / 16);  // 16-byte chunks of the longest slice
+  if (vec && p->max_len <= 32 && chunks <= 32 * 8) {
     for (int64_t l0 = 0; l0 < p->layers; l0 += kLayersPerLaunch) {
       const int nl = static_cast<int>(std::min<int64_t>(kLayersPerLaunch, p->layers - l0));
       for (int i = 0; i < nl; ++i) {
@@ -184,8 +195,12 @@ extern "C" int gorgon_kv_trim(const gorgon_kv_trim_params* p, void* stream) {
         a.dst[0][i] = p->k_dst ? p->k_dst[l0 + i] : p->k_src[l0 + i];
         a.dst[1][i] = p->v_dst ? p->v_dst[l0 + i] : p->v_src[l0 + i];
       }
-      dim3 grid(static_cast<unsigned>((p->heads + kWarps - 1) / kWarps), static_cast<unsigned>(p->batch), 2u * nl);
-      kv_trim_warp_kernel<<<grid, kWarps * 32, 0, st>>>(a, static_cast<int>(p->heads));
+      dim3 grid(static_cast<unsigned>((p->heads + kWarps - 1) / kWarps), static_cast<unsigned>(p->batch),
+                static_cast<unsigned>(nl));
+      if (chunks <= 32 * 4)
+        kv_trim_warp_kernel<4><<<grid, kWarps * 32, 0, st>>>(a, static_cast<int>(p->heads));
+      else
+        kv_trim_warp_kernel<8><<<grid, kWarps * 32, 0, st>>>(a, static_cast<int>(p->heads));
       int rc = check_cuda(cudaGetLastError(), "kv_trim launch");
       if (rc) return rc;
     }
